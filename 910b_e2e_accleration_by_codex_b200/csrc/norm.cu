@@ -1,0 +1,101 @@
+// a4. Gated RMSNorm: y = rnd(w * rnd(x * rsqrt(mean(x^2) + eps))) * silu(gate), one warp per row.
+// Follows Qwen3_5RMSNormGated.forward (transformers modeling_qwen3_5.py:181-191): the statistics are
+// fp32, the normalised row is rounded to the activation dtype before the weight multiply (which is
+// itself a dtype op), and the gate product is fp32 with a final rounding.
+#include "common.cuh"
+
+namespace gdn {
+
+template <typename T, bool VEC>
+__global__ void __launch_bounds__(256) gated_rmsnorm_kernel(const T* __restrict__ x, int64_t x_rs,
+                                                            const T* __restrict__ gate, int64_t g_rs,
+                                                            const T* __restrict__ w, T* __restrict__ y,
+                                                            int64_t y_rs, int64_t rows, int dim, float eps) {
+  const int64_t row = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const T* xr = x + row * x_rs;
+  const T* gr = gate + row * g_rs;
+  T* yr = y + row * y_rs;
+  constexpr int G = 8;  // up to 8 groups of 4 per lane: dim <= 1024
+  float4 xv[G];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < G; ++i) {
+    const int c = (i * 32 + lane) * 4;
+    if (c < dim) {
+      if (VEC) {
+        xv[i] = ld4<T>(xr + c);
+      } else {
+        xv[i] = make_float4(Io<T>::ld(xr + c), Io<T>::ld(xr + c + 1), Io<T>::ld(xr + c + 2),
+                            Io<T>::ld(xr + c + 3));
+      }
+      ss += xv[i].x * xv[i].x + xv[i].y * xv[i].y + xv[i].z * xv[i].z + xv[i].w * xv[i].w;
+    }
+  }
+  ss = warp_sum(ss);
+  const float r = 1.0f / sqrtf(ss / float(dim) + eps);
+#pragma unroll
+  for (int i = 0; i < G; ++i) {
+    const int c = (i * 32 + lane) * 4;
+    if (c < dim) {
+      float4 gv, wv;
+      if (VEC) {
+        gv = ld4<T>(gr + c);
+        wv = ld4<T>(w + c);
+      } else {
+        gv = make_float4(Io<T>::ld(gr + c), Io<T>::ld(gr + c + 1), Io<T>::ld(gr + c + 2),
+                         Io<T>::ld(gr + c + 3));
+        wv = make_float4(Io<T>::ld(w + c), Io<T>::ld(w + c + 1), Io<T>::ld(w + c + 2),
+                         Io<T>::ld(w + c + 3));
+      }
+      float4 o;
+      o.x = Io<T>::rnd(wv.x * Io<T>::rnd(xv[i].x * r)) * silu_f(gv.x);
+      o.y = Io<T>::rnd(wv.y * Io<T>::rnd(xv[i].y * r)) * silu_f(gv.y);
+      o.z = Io<T>::rnd(wv.z * Io<T>::rnd(xv[i].z * r)) * silu_f(gv.z);
+      o.w = Io<T>::rnd(wv.w * Io<T>::rnd(xv[i].w * r)) * silu_f(gv.w);
+      if (VEC) {
+        st4<T>(yr + c, o);
+      } else {
+        Io<T>::st(yr + c, o.x);
+        Io<T>::st(yr + c + 1, o.y);
+        Io<T>::st(yr + c + 2, o.z);
+        Io<T>::st(yr + c + 3, o.w);
+      }
+    }
+  }
+}
+
+template <typename T>
+static int launch_norm(const void* x, int64_t x_rs, const void* gate, int64_t g_rs, const void* w,
+                       void* y, int64_t y_rs, int64_t rows, int dim, float eps, cudaStream_t s) {
+  const size_t vb = 4 * sizeof(T);
+  const bool vec = aligned(x, vb) && aligned(gate, vb) && aligned(w, vb) && aligned(y, vb) &&
+                   (x_rs % 4 == 0) && (g_rs % 4 == 0) && (y_rs % 4 == 0);
+  const int threads = 256;
+  const int64_t blocks = (rows * 32 + threads - 1) / threads;
+  if (vec)
+    gated_rmsnorm_kernel<T, true><<<dim3(unsigned(blocks)), threads, 0, s>>>(
+        (const T*)x, x_rs, (const T*)gate, g_rs, (const T*)w, (T*)y, y_rs, rows, dim, eps);
+  else
+    gated_rmsnorm_kernel<T, false><<<dim3(unsigned(blocks)), threads, 0, s>>>(
+        (const T*)x, x_rs, (const T*)gate, g_rs, (const T*)w, (T*)y, y_rs, rows, dim, eps);
+  return check_launch("gdn_gated_rmsnorm");
+}
+
+}  // namespace gdn
+
+extern "C" int gdn_gated_rmsnorm(const void* x, int64_t x_rs, const void* gate, int64_t g_rs,
+                                 const void* weight, void* y, int64_t y_rs, int64_t rows, int dim,
+                                 float eps, int dtype, void* stream) {
+  using namespace gdn;
+  if (rows < 0 || dim <= 0) return fail(GDN_ERR_ARG, "gdn_gated_rmsnorm: rows=%lld dim=%d", (long long)rows, dim);
+  if (rows == 0) return GDN_OK;
+  if (!x || !gate || !weight || !y) return fail(GDN_ERR_ARG, "gdn_gated_rmsnorm: null pointer");
+  if (dim % 4 != 0 || dim > 1024) return fail(GDN_ERR_SHAPE, "gdn_gated_rmsnorm: dim=%d (need %%4==0, <=1024)", dim);
+  if (rows > (int64_t(1) << 36)) return fail(GDN_ERR_ARG, "gdn_gated_rmsnorm: rows too large");
+  cudaStream_t s = as_stream(stream);
+  if (dtype == GDN_BF16) return launch_norm<__nv_bfloat16>(x, x_rs, gate, g_rs, weight, y, y_rs, rows, dim, eps, s);
+  if (dtype == GDN_F32) return launch_norm<float>(x, x_rs, gate, g_rs, weight, y, y_rs, rows, dim, eps, s);
+  return fail(GDN_ERR_DTYPE, "gdn_gated_rmsnorm: dtype %d", dtype);
+}

@@ -1,0 +1,312 @@
+"""Torch-facing GDN operators backed by the CUDA library (C ABI in include/gdn_b200.h).
+
+Two groups of functions:
+
+* Drop-ins with the reference's signatures, for installation on HF modules by
+  ``patch.patch_model`` exactly where the reference installs its own:
+    - ``chunk_gated_delta_rule``      (src/gdn_chunk_fast2.py:11-12, transformers :234-244)
+    - ``recurrent_gated_delta_rule``  (src/recurrent_single_step.py:8-9, transformers :314-316)
+    - ``causal_conv1d_update``        (transformers :210-216)
+    - ``elem_conv_update``            (src/cb_engine.py:43)
+    - ``gated_rmsnorm`` / ``rmsnorm_gated_forward`` (transformers :181, src/cb_engine.py:65)
+  They allocate their outputs like the reference functions do.
+* Slot-indexed operators used by the engine (``engine.CBEngine``): state pools are read
+  and written in place through a slot index inside the kernels, and nothing is
+  allocated, so the calls can be captured in CUDA graphs.
+
+Every call runs on ``torch.cuda.current_stream()``.  Failures raise RuntimeError with
+the library's message.  There is no CPU path: CPU tensors raise.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import _lib
+from ._lib import GDN_BF16, GDN_CONV_ELEM, GDN_CONV_HF, GDN_F32
+
+_DT = {torch.bfloat16: GDN_BF16, torch.float32: GDN_F32}
+
+
+def _dtype_code(t: torch.Tensor) -> int:
+    try:
+        return _DT[t.dtype]
+    except KeyError:
+        raise TypeError(f"GDN kernels take bfloat16 or float32 activations, got {t.dtype}") from None
+
+
+def _need_cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError("GDN operators run on CUDA tensors only (no CPU fallback)")
+
+
+def _p(t):
+    return None if t is None else t.data_ptr()
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _rows(t: torch.Tensor, d: int) -> torch.Tensor:
+    """View as [..., d] with unit stride in the last dim and heads packed (stride d)."""
+    if t.stride(-1) != 1 or (t.dim() >= 2 and t.shape[-2] > 1 and t.stride(-2) != d):
+        t = t.contiguous()
+    return t
+
+
+def _i32(t):
+    if t is None:
+        return None
+    if t.dtype != torch.int32 or not t.is_contiguous():
+        t = t.to(torch.int32).contiguous()
+    return t
+
+
+# ============================================================================ a4: gated RMSNorm
+def gated_rmsnorm(x: torch.Tensor, gate: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6,
+                  out: torch.Tensor | None = None) -> torch.Tensor:
+    """Qwen3_5RMSNormGated.forward (transformers modeling_qwen3_5.py:181-191):
+    y = weight * rnd(x * rsqrt(mean(x^2) + eps)) * silu(gate), in x's dtype."""
+    _need_cuda(x, gate, weight)
+    dim = x.shape[-1]
+    x2 = x.reshape(-1, dim)
+    if x2.stride(-1) != 1:
+        x2 = x2.contiguous()
+    g2 = gate.to(x.dtype).reshape(-1, dim)
+    if g2.stride(-1) != 1:
+        g2 = g2.contiguous()
+    w = weight.to(x.dtype).contiguous()
+    y = torch.empty_like(x2) if out is None else out.view(-1, dim)
+    lib = _lib.load()
+    _lib.check(lib.gdn_gated_rmsnorm(_p(x2), x2.stride(0), _p(g2), g2.stride(0), _p(w), _p(y), y.stride(0),
+                                     x2.shape[0], dim, float(eps), _dtype_code(x), _stream()),
+               "gdn_gated_rmsnorm")
+    return y.view(x.shape)
+
+
+def rmsnorm_gated_forward(self, hidden_states, gate=None):
+    """Bound in place of Qwen3_5RMSNormGated.forward (src/cb_engine.py:65-67, 72-73)."""
+    return gated_rmsnorm(hidden_states, gate, self.weight, self.variance_epsilon)
+
+
+# ============================================================================ a3: decode conv
+def _conv_update(x, state, weight, bias, mode, slot_idx=None, out=None, err=None):
+    _need_cuda(x, state, weight, bias)
+    if x.dim() == 2:
+        x = x.unsqueeze(-1)
+    B, Cc, T = x.shape
+    K = state.shape[-1]
+    if weight.dim() == 3:
+        weight = weight.squeeze(1)
+    if weight.shape != (Cc, K):
+        raise ValueError(f"conv weight {tuple(weight.shape)} != ({Cc}, {K})")
+    wd = weight.dtype
+    if x.dtype != wd:
+        x = x.to(wd)
+    if state.dtype != wd or not state.is_contiguous():
+        raise ValueError("conv state must be a contiguous tensor of the weight's dtype (updated in place)")
+    w = weight.contiguous()
+    b = None if bias is None else bias.to(wd).contiguous()
+    y = torch.empty(B, Cc, T, dtype=wd, device=x.device) if out is None else out
+    n_slots = state.shape[0]
+    lib = _lib.load()
+    _lib.check(lib.gdn_conv_update(_p(x), x.stride(0), x.stride(1), x.stride(2), _p(state), _p(_i32(slot_idx)),
+                                   n_slots, _p(w), _p(b), _p(y), y.stride(0), y.stride(1), y.stride(2), B, Cc, T,
+                                   K, 1, mode, _dtype_code(w), _p(err), _stream()), "gdn_conv_update")
+    return y
+
+
+def causal_conv1d_update(hidden_states, conv_state, weight, bias=None, activation=None):
+    """torch_causal_conv1d_update (transformers modeling_qwen3_5.py:210-226): conv_state [B,C,K]
+    updated in place; returns silu(conv) [B,C,T] in hidden_states' dtype (the HF fallback applies
+    silu whatever `activation` says)."""
+    y = _conv_update(hidden_states, conv_state, weight, bias, GDN_CONV_HF)
+    return y.to(hidden_states.dtype)
+
+
+def elem_conv_update(x, state, weight, bias):
+    """elem_conv_update (src/cb_engine.py:43-51): x [n,C,1], state [n,C,K] updated in place;
+    products and sum rounded in the weight dtype as the reference's mul + sum does."""
+    y = _conv_update(x, state, weight, bias, GDN_CONV_ELEM)
+    return y.to(x.dtype)
+
+
+# ============================================================================ a2: recurrence
+def recurrent_gated_delta_rule(query, key, value, g, beta, initial_state, output_final_state,
+                               use_qk_l2norm_in_kernel=False):
+    """recurrent_single_step / torch_recurrent_gated_delta_rule (src/recurrent_single_step.py:8-32,
+    transformers modeling_qwen3_5.py:314-353).  query/key [B,T,Hq,dk] (Hq divides Hv; HF passes
+    them repeated to Hv heads), value [B,T,Hv,dv], g/beta [B,T,Hv].  Returns (out [B,T,Hv,dv] in
+    query's dtype, new fp32 state [B,Hv,dk,dv] or None)."""
+    _need_cuda(query, key, value, g, beta, initial_state)
+    dt = query.dtype
+    B, T, Hq, dk = query.shape
+    Hv, dv = value.shape[2], value.shape[3]
+    q = _rows(query, dk)
+    k = _rows(key.to(dt), dk)
+    v = _rows(value.to(dt), dv)
+    gg = g.to(torch.float32).contiguous()
+    bb = beta.to(torch.float32).contiguous()
+    init = None if initial_state is None else initial_state.to(torch.float32).contiguous()
+    final = torch.empty(B, Hv, dk, dv, dtype=torch.float32, device=query.device) if output_final_state else None
+    out = torch.empty(B, T, Hv, dv, dtype=dt, device=query.device)
+    lib = _lib.load()
+    _lib.check(lib.gdn_recurrent(_p(q), q.stride(0), q.stride(1), _p(k), k.stride(0), k.stride(1), _p(v),
+                                 v.stride(0), v.stride(1), _p(gg), _p(bb), T * Hv, Hv, _p(init), None,
+                                 _p(final), None, B, _p(out), T * Hv * dv, Hv * dv, B, T, Hq, Hv, dk, dv,
+                                 int(bool(use_qk_l2norm_in_kernel)), _dtype_code(q), None, _stream()),
+               "gdn_recurrent")
+    return out, final
+
+
+def recurrent_step_slots(q, k, v, g, beta, state_pool, slot_idx, use_qk_l2norm=True, out=None, err=None):
+    """One decode token per sequence with the state gathered from and scattered back to
+    ``state_pool[slot_idx]`` inside the kernel (replaces src/cb_engine.py:344-347).
+    q,k [n,Hk,dk], v [n,Hv,dv], g/beta [n,Hv] fp32, state_pool [S,Hv,dk,dv] fp32."""
+    _need_cuda(q, k, v, g, beta, state_pool, slot_idx)
+    n, Hk, dk = q.shape
+    Hv, dv = v.shape[1], v.shape[2]
+    q, k, v = _rows(q, dk), _rows(k, dk), _rows(v, dv)
+    g = g.to(torch.float32)
+    beta = beta.to(torch.float32)
+    if g.stride(-1) != 1 or beta.stride(-1) != 1 or g.stride(0) != beta.stride(0):
+        g, beta = g.contiguous(), beta.contiguous()
+    o = torch.empty(n, Hv, dv, dtype=q.dtype, device=q.device) if out is None else out
+    si = _i32(slot_idx)
+    lib = _lib.load()
+    _lib.check(lib.gdn_recurrent(_p(q), q.stride(0), 0, _p(k), k.stride(0), 0, _p(v), v.stride(0), 0, _p(g),
+                                 _p(beta), g.stride(0), 0, _p(state_pool), _p(si), _p(state_pool), _p(si),
+                                 state_pool.shape[0], _p(o), o.stride(0), 0, n, 1, Hk, Hv, dk, dv,
+                                 int(bool(use_qk_l2norm)), _dtype_code(q), _p(err), _stream()),
+               "gdn_recurrent")
+    return o
+
+
+# ============================================================================ a1: chunk prefill
+def chunk_gated_delta_rule(query, key, value, g, beta, chunk_size=64, initial_state=None,
+                           output_final_state=False, use_qk_l2norm_in_kernel=False):
+    """fast_chunk_gated_delta_rule_v2 (src/gdn_chunk_fast2.py:11-62) / torch_chunk_gated_delta_rule
+    (transformers modeling_qwen3_5.py:234-311).  [B,L,H,D] inputs of equal length L; returns
+    (out [B,L,Hv,dv] in query's dtype, final fp32 state [B,Hv,dk,dv] or None).  The kernels use
+    64-token chunks whatever ``chunk_size`` says (the chunked form is exact algebra; chunk size
+    only changes fp32 rounding)."""
+    _need_cuda(query, key, value, g, beta, initial_state)
+    if chunk_size <= 0:
+        raise ValueError(f"chunk_size must be positive, got {chunk_size}")
+    dt = query.dtype
+    B, L, Hq, dk = query.shape
+    Hv, dv = value.shape[2], value.shape[3]
+    out = torch.empty(B, L, Hv, dv, dtype=dt, device=query.device)
+    final = torch.empty(B, Hv, dk, dv, dtype=torch.float32, device=query.device) if output_final_state else None
+    init = None if initial_state is None else initial_state.to(torch.float32).contiguous()
+    if B == 0 or L == 0:
+        if final is not None:
+            final.copy_(init if init is not None else torch.zeros_like(final))
+        return out, final
+    q = query.contiguous()
+    k = key.to(dt).contiguous()
+    v = value.to(dt).contiguous()
+    gg = g.to(torch.float32).contiguous()
+    bb = beta.to(torch.float32).contiguous()
+    cu = torch.arange(0, B + 1, dtype=torch.int32, device=query.device) * L
+    lib = _lib.load()
+    _lib.check(lib.gdn_chunk_prefill(_p(q), Hq * dk, _p(k), Hq * dk, _p(v), Hv * dv, _p(gg), _p(bb), Hv, _p(cu),
+                                     B, B * L, _p(init), None, None, _p(final), None, B, _p(out), Hv * dv, Hq,
+                                     Hv, dk, dv, int(bool(use_qk_l2norm_in_kernel)), _dtype_code(q), None,
+                                     _stream()), "gdn_chunk_prefill")
+    return out, final
+
+
+def chunk_prefill_varlen(q, k, v, g, beta, cu_seqlens, state_pool=None, slot_idx=None, use_initial=None,
+                         use_qk_l2norm=True, out=None, err=None):
+    """Packed varlen chunk prefill.  q,k [T,Hk,dk], v [T,Hv,dv] (token strides may be wider than
+    the head block, e.g. column slices of the conv output), g/beta [T,Hv] fp32, cu_seqlens
+    int32 [B+1] (device).  Sequence b starts from state_pool[slot_idx[b]] where use_initial[b]
+    (else zeros) and its final state is written to state_pool[slot_idx[b]]."""
+    _need_cuda(q, k, v, g, beta, cu_seqlens, state_pool)
+    T, Hk, dk = q.shape
+    Hv, dv = v.shape[1], v.shape[2]
+    for t, d in ((q, dk), (k, dk), (v, dv)):
+        if t.stride(-1) != 1 or t.stride(-2) != d:
+            raise ValueError("q/k/v must have packed heads and unit stride in the last dim")
+    g = g.to(torch.float32)
+    beta = beta.to(torch.float32)
+    if g.stride(-1) != 1 or beta.stride(-1) != 1 or g.stride(0) != beta.stride(0):
+        g, beta = g.contiguous(), beta.contiguous()
+    o = torch.empty(T, Hv, dv, dtype=q.dtype, device=q.device) if out is None else out
+    B = cu_seqlens.numel() - 1
+    si = _i32(slot_idx)
+    ui = _i32(use_initial)
+    # no use_initial: every sequence starts from zeros (the C ABI reads the pool only when given it)
+    init_pool = None if use_initial is None else state_pool
+    lib = _lib.load()
+    _lib.check(lib.gdn_chunk_prefill(_p(q), q.stride(0), _p(k), k.stride(0), _p(v), v.stride(0), _p(g), _p(beta),
+                                     g.stride(0), _p(_i32(cu_seqlens)), B, T, _p(init_pool), _p(si), _p(ui),
+                                     _p(state_pool), _p(si), 0 if state_pool is None else state_pool.shape[0],
+                                     _p(o), o.stride(0), Hk, Hv, dk, dv, int(bool(use_qk_l2norm)),
+                                     _dtype_code(q), _p(err), _stream()), "gdn_chunk_prefill")
+    return o
+
+
+# ============================================================================ prefill conv
+def prefill_conv_varlen(x, cu_seqlens, weight, bias=None, conv_pool=None, slot_idx=None, use_initial=None,
+                        out=None, err=None):
+    """Varlen causal conv1d + silu over packed tokens x [T,C] (transformers :463-474,
+    src/cb_tp.py:158-164 and :236-244); conv state carried from / written to conv_pool[slot_idx]."""
+    _need_cuda(x, cu_seqlens, weight, bias, conv_pool)
+    T, Cc = x.shape
+    if x.stride(1) != 1:
+        x = x.contiguous()
+    if weight.dim() == 3:
+        weight = weight.squeeze(1)
+    K = weight.shape[-1]
+    w = weight.to(x.dtype).contiguous()
+    b = None if bias is None else bias.to(x.dtype).contiguous()
+    y = torch.empty_like(x) if out is None else out
+    B = cu_seqlens.numel() - 1
+    lib = _lib.load()
+    _lib.check(lib.gdn_prefill_conv(_p(x), x.stride(0), _p(y), y.stride(0), _p(_i32(cu_seqlens)), B, _p(conv_pool),
+                                    _p(_i32(slot_idx)), _p(_i32(use_initial)),
+                                    0 if conv_pool is None else conv_pool.shape[0], _p(w), _p(b), Cc, K, 1,
+                                    _dtype_code(x), _p(err), _stream()), "gdn_prefill_conv")
+    return y
+
+
+# ============================================================================ fused decode layer
+def decode_layer_workspace(n, Hk, Hv, dk, dv, dtype, device):
+    """Device workspace for ``decode_layer`` (the conv output between its two kernels)."""
+    nbytes = _lib.load().gdn_decode_layer_workspace_size(n, Hk, Hv, dk, dv, _DT[dtype])
+    return torch.empty(nbytes, dtype=torch.uint8, device=device)
+
+
+def decode_layer(mixed_qkv, z, a, b, A_log, dt_bias, conv_w, conv_b, conv_pool, rec_pool, slot_idx, norm_w,
+                 eps, Hk, Hv, dk, dv, conv_mode=GDN_CONV_ELEM, workspace=None, out=None, err=None):
+    """The operator part of CBEngine._gdn (src/cb_engine.py:318-352) for n slots in one call:
+    conv update (conv_pool[slot_idx] in place) -> gates -> l2norm -> recurrence
+    (rec_pool[slot_idx] in place) -> gated RMSNorm.  mixed_qkv [n,C], z [n,Hv,dv], a/b [n,Hv],
+    A_log/dt_bias [Hv] fp32.  Returns out [n,Hv,dv]."""
+    _need_cuda(mixed_qkv, z, a, b, A_log, dt_bias, conv_w, conv_pool, rec_pool, slot_idx, norm_w)
+    n, Cc = mixed_qkv.shape[0], mixed_qkv.shape[-1]
+    mixed = mixed_qkv.reshape(n, Cc)
+    if mixed.stride(1) != 1:
+        mixed = mixed.contiguous()
+    K = conv_pool.shape[-1]
+    if workspace is None:
+        workspace = decode_layer_workspace(n, Hk, Hv, dk, dv, mixed.dtype, mixed.device)
+    o = torch.empty(n, Hv, dv, dtype=mixed.dtype, device=mixed.device) if out is None else out
+    w = conv_w.squeeze(1) if conv_w.dim() == 3 else conv_w
+    lib = _lib.load()
+    _lib.check(lib.gdn_decode_layer(_p(mixed), mixed.stride(0), _p(z), _p(a), _p(b), _p(A_log), _p(dt_bias), _p(w),
+                                    _p(conv_b), _p(conv_pool), _p(rec_pool), _p(_i32(slot_idx)), rec_pool.shape[0],
+                                    _p(norm_w), float(eps), _p(o), n, Hk, Hv, dk, dv, K, conv_mode, _p(workspace),
+                                    workspace.numel(), _dtype_code(mixed), _p(err), _stream()),
+               "gdn_decode_layer")
+    return o
+
+
+def l2_scale(dk: int) -> float:
+    """The q scale the reference applies after l2norm (1/sqrt(dk))."""
+    return 1.0 / math.sqrt(dk)

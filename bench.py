@@ -1,0 +1,444 @@
+#!/usr/bin/env python
+"""Benchmark of the GDN hot path on B200.
+
+Headline: one GDN chunk-prefill layer over 16 packed ragged sequences
+(lengths U[200,1200], seeded), 16 q/k heads x 128, 48 v heads x 128, chunk 64, bf16 q/k/v,
+beta/g on the bf16 grid, fp32 recurrent state N(0, 0.02) read from and written back to a
+slot pool.  One step = one call of the slot-indexed chunk-prefill entry point over the whole
+batch.  ``value`` = tokens/s with inputs resident in HBM; ``e2e`` = the same through the
+public API with the step's inputs copied from pinned host memory and its output copied back,
+inside the timed region.
+
+Also reported (``decode``): one 16-slot decode step over 48 GDN layers
+(fused conv + gates + recurrence + gated RMSNorm per layer, slot-indexed pools), replayed from a
+CUDA graph, in microseconds per step with its HBM roofline.
+
+``--impl reference`` times the CPU restatement of the reference's torch path (the oracle
+port) on this host's cores over a bounded sample of the same workload.
+
+Multi-GPU (torchrun, one rank per GPU): every rank runs its own replica of the workload
+(weak scaling, no collective on the data path); value = all ranks' tokens / max rank time.
+"""
+from __future__ import annotations
+
+import argparse
+import importlib
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+PKG = "910b_e2e_accleration_by_codex_b200"
+METRIC = "GDN chunk-prefill tokens/s & 16-slot decode-step µs; % of roofline"
+
+HK, HV, D, CHUNK = 16, 48, 128, 64
+N_SEQ, LMIN, LMAX = 16, 200, 1200
+# algorithmic FLOPs per (value head, 64-token chunk), dense chunk form, d=128:
+# 2C^2d*5 (KK^T, QK^T, T.Vb, T.Kb, QK.vn) + 2Cd^2*3 (W.S, Qg.S, Kd^T.vn) + 2C^3/3 (inverse)
+FLOP_PER_HEAD_CHUNK = 2 * CHUNK * CHUNK * D * 5 + 2 * CHUNK * D * D * 3 + 2 * CHUNK ** 3 / 3
+# decode config 2
+DEC_LAYERS, DEC_SLOTS, CONV_K = 48, 16, 4
+CONV_DIM = 2 * HK * D + HV * D
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--no-decode", action="store_true", help="skip the config-2 decode measurement")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0, help="target CPU-baseline sample time")
+    return ap.parse_args()
+
+
+# ----------------------------------------------------------------------------- workload
+def make_prefill_workload(seed: int):
+    """Config-1 inputs on the host (CPU tensors)."""
+    g = torch.Generator().manual_seed(seed)
+    lens = torch.randint(LMIN, LMAX + 1, (N_SEQ,), generator=g).tolist()
+    T = sum(lens)
+    q = torch.randn(T, HK, D, generator=g)
+    k = torch.randn(T, HK, D, generator=g)
+    q = (q / q.norm(dim=-1, keepdim=True)).to(torch.bfloat16)
+    k = (k / k.norm(dim=-1, keepdim=True)).to(torch.bfloat16)
+    v = torch.randn(T, HV, D, generator=g).to(torch.bfloat16)
+    beta = torch.sigmoid(torch.randn(T, HV, generator=g)).to(torch.bfloat16).float()
+    gg = (-(0.01 + 0.99 * torch.rand(T, HV, generator=g))).to(torch.bfloat16).float()
+    init = torch.randn(N_SEQ, HV, D, D, generator=g) * 0.02
+    cu = torch.tensor([0] + np.cumsum(lens).tolist(), dtype=torch.int32)
+    return dict(lens=lens, T=T, q=q, k=k, v=v, g=gg, beta=beta, init=init, cu=cu)
+
+
+def prefill_flops(lens):
+    chunks = sum(math.ceil(L / CHUNK) for L in lens)
+    return chunks * HV * FLOP_PER_HEAD_CHUNK, chunks
+
+
+def prefill_bytes(w):
+    """Algorithmic HBM bytes per launch: q,k (un-repeated), v, beta, g in; o out; state r+w."""
+    T = w["T"]
+    per_tok = (2 * HK * D + HV * D) * 2 + 2 * HV * 4 + HV * D * 2
+    return T * per_tok + 2 * N_SEQ * HV * D * D * 4
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi sampled every 100 ms while the benchmark runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.proc = None
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
+                 "-i", str(gpu_index)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for n_, val in zip(names, f[5:9]):
+                if val.lower() == "active":
+                    reasons.add(n_)
+        if not sm:
+            return None
+        busy = [s for s in sm if s > 0.5 * max(sm)] or sm
+        return {"sm_mhz": statistics.median(busy), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------- distributed
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        if args.impl == "ours":
+            torch.cuda.set_device(local)
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                    device_id=torch.device("cuda", local))
+        else:
+            dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def allreduce_max(x: float, world: int) -> float:
+    if world <= 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def allreduce_sum(x: float, world: int) -> float:
+    if world <= 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+# ----------------------------------------------------------------------------- CPU legs
+def cpu_prefill_sample(w, seconds: float):
+    """Run the oracle (CPU restatement of src/gdn_chunk_fast2.py, one sequence per call as
+    TPEngine.prefill does) over the workload's sequences in order until ~`seconds` elapse."""
+    from oracle import gdn_oracle as O
+    r = HV // HK
+    toks, used, el = 0, 0, 0.0
+    t0 = time.perf_counter()
+    for b, L in enumerate(w["lens"]):
+        s, e = int(w["cu"][b]), int(w["cu"][b + 1])
+        q = O.repeat_heads(w["q"][s:e].float().numpy(), r)[None]
+        k = O.repeat_heads(w["k"][s:e].float().numpy(), r)[None]
+        O.chunk_gated_delta_rule(q, k, w["v"][s:e].float().numpy()[None], w["g"][s:e].numpy()[None],
+                                 w["beta"][s:e].numpy()[None], 64, w["init"][b].numpy()[None], True, True, "bf16")
+        toks += L
+        used += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    return toks / el, f"{used} of {len(w['lens'])} sequences ({toks} tokens), one oracle call per sequence", el
+
+
+def cpu_cores() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def run_reference(args, world, rank):
+    """--impl reference: the oracle port of the reference's torch path on the host cores."""
+    if rank != 0:
+        return
+    w = make_prefill_workload(args.seed)
+    torch.set_num_threads(cpu_cores())
+    for _ in range(max(0, min(args.warmup, 1))):
+        cpu_prefill_sample(w, 0.0)
+    vals, samples, secs = [], None, 0.0
+    per_step = max(2.0, min(20.0, 120.0 / max(1, args.steps)))
+    for _ in range(args.steps):
+        v, samples, el = cpu_prefill_sample(w, per_step)
+        vals.append(v)
+        secs += el
+    value = statistics.median(vals)
+    line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1000.0 * w["T"] / value, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "impl": "reference",
+            "config": {"workload": "config1: GDN chunk prefill, 16 ragged seqs U[200,1200], Hk=16 Hv=48 d=128",
+                       "total_tokens": w["T"], "parallelism": "cpu"},
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cpu_cores(), "kind": "port",
+                             "sample": samples},
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------- GPU legs
+def time_events(fn, steps, stream):
+    """Run fn() `steps` times on `stream`; returns per-step CUDA-event durations in ms."""
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for a, b in evs:
+        a.record(stream)
+        fn()
+        b.record(stream)
+    torch.cuda.synchronize()
+    return [a.elapsed_time(b) for a, b in evs]
+
+
+def load_traffic():
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    try:
+        with open(path) as f:
+            return json.load(f)
+    except (OSError, ValueError):
+        return {}
+
+
+def run_ours(args, world, rank, local):
+    ops = importlib.import_module(f"{PKG}.ops")
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except (OSError, ValueError):
+        pass
+    hbm_peak = peaks.get("hbm_gbs", 6650.0)
+    tc_peak = peaks.get("bf16_tflops", 1590.0)
+    peak_src = "of measured" if peaks else "of fallback"
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.current_stream()
+    w = make_prefill_workload(args.seed + rank)
+    T = w["T"]
+    # ---- device-resident inputs
+    q, k, v = w["q"].to(dev), w["k"].to(dev), w["v"].to(dev)
+    g, beta = w["g"].to(dev), w["beta"].to(dev)
+    cu = w["cu"].to(dev)
+    pool = w["init"].to(dev).contiguous()
+    slot = torch.arange(N_SEQ, dtype=torch.int32, device=dev)
+    use_init = torch.ones(N_SEQ, dtype=torch.int32, device=dev)
+    out = torch.empty(T, HV, D, dtype=torch.bfloat16, device=dev)
+
+    def step():
+        ops.chunk_prefill_varlen(q, k, v, g, beta, cu, pool, slot, use_init, True, out=out)
+
+    clocks = ClockSampler(local)
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    durs = time_events(step, args.steps, stream)
+    barrier(world)
+    torch.cuda.synchronize()
+    ms = sum(durs) / len(durs)
+    ms_max = allreduce_max(ms, world)
+    tot_tokens = allreduce_sum(float(T), world)
+    value = tot_tokens / (ms_max / 1e3)
+
+    # ---- e2e through the public API with pinned host buffers
+    hq, hk, hv = w["q"].pin_memory(), w["k"].pin_memory(), w["v"].pin_memory()
+    hg, hb = w["g"].pin_memory(), w["beta"].pin_memory()
+    hout = torch.empty(T, HV, D, dtype=torch.bfloat16).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv, hg, hb))
+    d2h = hout.numel() * hout.element_size()
+
+    def e2e_step():
+        q.copy_(hq, non_blocking=True)
+        k.copy_(hk, non_blocking=True)
+        v.copy_(hv, non_blocking=True)
+        g.copy_(hg, non_blocking=True)
+        beta.copy_(hb, non_blocking=True)
+        ops.chunk_prefill_varlen(q, k, v, g, beta, cu, pool, slot, use_init, True, out=out)
+        hout.copy_(out, non_blocking=True)
+
+    for _ in range(max(1, min(args.warmup, 3))):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier(world)
+    e2e_durs = time_events(e2e_step, args.steps, stream)
+    barrier(world)
+    e2e_ms = allreduce_max(sum(e2e_durs) / len(e2e_durs), world)
+    e2e_value = tot_tokens / (e2e_ms / 1e3)
+
+    # ---- decode (config 2): 48 layers x 16 slots, CUDA-graph replay
+    decode = None
+    if not args.no_decode:
+        decode = run_decode(ops, dev, args, world, hbm_peak, peak_src)
+    clk = clocks.stop()
+
+    flops, chunks = prefill_flops(w["lens"])
+    achieved_tflops = flops / (ms / 1e3) / 1e12
+    traffic = load_traffic().get("gdn_chunk_prefill")
+    algo_bytes = prefill_bytes(w)
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded; config-1 distributions; no dataset or weights needed)",
+        "config": {"workload": "config1: GDN chunk prefill, 16 packed ragged seqs U[200,1200], Hk=16 Hv=48 "
+                               "dk=dv=128, chunk 64, bf16 q/k/v, fp32 state N(0,0.02) from a slot pool",
+                   "total_tokens_per_gpu": T, "chunks_per_head": chunks,
+                   "l2": f"inputs larger than L2 ({algo_bytes / 1e6:.0f} MB touched per step > 126 MB)",
+                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
+        "roofline": {"bound": "tensor", "achieved": achieved_tflops, "peak": tc_peak, "unit": "TFLOP/s",
+                     "frac": achieved_tflops / tc_peak, "peak_source": peak_src + " (bf16 burst)",
+                     "traffic": traffic, "algorithmic_flops_per_launch": flops,
+                     "algorithmic_bytes_per_launch": algo_bytes,
+                     "hbm_frac": algo_bytes / (ms / 1e3) / 1e9 / hbm_peak},
+        "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "gpu_launches": args.steps,
+        "clocks": clk,
+    }
+    if decode is not None:
+        line["decode"] = decode
+        line["gpu_launches"] += decode["gpu_launches"]
+    if rank == 0 and world == 1 and not args.no_cpu:
+        torch.set_num_threads(cpu_cores())
+        v_cpu, sample, el = cpu_prefill_sample(w, args.cpu_seconds)
+        line["cpu_baseline"] = {"value": v_cpu, "unit": "tokens/s", "cores": cpu_cores(), "kind": "port",
+                                "sample": sample + f", {el:.1f} s"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def run_decode(ops, dev, args, world, hbm_peak, peak_src):
+    g = torch.Generator(device="cpu").manual_seed(1234)
+    n, L = DEC_SLOTS, DEC_LAYERS
+    bf = torch.bfloat16
+    layers = []
+    for _ in range(L):
+        layers.append(dict(
+            conv_w=(torch.rand(CONV_DIM, CONV_K, generator=g) - 0.5).to(bf).to(dev),
+            A_log=torch.log(torch.empty(HV).uniform_(1, 16, generator=g)).to(dev),
+            dt_bias=(torch.rand(HV, generator=g) * 2 - 1).to(dev),
+            norm_w=(1 + 0.1 * torch.randn(D, generator=g)).to(bf).to(dev),
+            conv_pool=torch.randn(n, CONV_DIM, CONV_K, generator=g).to(bf).to(dev),
+            rec_pool=(torch.randn(n, HV, D, D, generator=g) * 0.02).to(dev),
+            mixed=torch.randn(n, CONV_DIM, generator=g).to(bf).to(dev),
+            z=torch.randn(n, HV, D, generator=g).to(bf).to(dev),
+            a=torch.randn(n, HV, generator=g).to(bf).to(dev),
+            b=torch.randn(n, HV, generator=g).to(bf).to(dev),
+            out=torch.empty(n, HV, D, dtype=bf, device=dev)))
+    slot = torch.randperm(n, generator=g).to(torch.int32).to(dev)
+    ws = ops.decode_layer_workspace(n, HK, HV, D, D, bf, dev)
+
+    def step():
+        for Ly in layers:
+            ops.decode_layer(Ly["mixed"], Ly["z"], Ly["a"], Ly["b"], Ly["A_log"], Ly["dt_bias"], Ly["conv_w"], None,
+                             Ly["conv_pool"], Ly["rec_pool"], slot, Ly["norm_w"], 1e-6, HK, HV, D, D,
+                             workspace=ws, out=Ly["out"])
+
+    step()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    cap = torch.cuda.Stream()
+    cap.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(cap):
+        with torch.cuda.graph(graph, stream=cap):
+            step()
+    torch.cuda.current_stream().wait_stream(cap)
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    barrier(world)
+    durs = time_events(graph.replay, args.steps, torch.cuda.current_stream())
+    barrier(world)
+    us = 1000.0 * sum(durs) / len(durs)
+    us_max = 1000.0 * allreduce_max(us / 1000.0, world)
+    state_bytes = 2 * L * n * HV * D * D * 4
+    conv_bytes = 2 * L * n * CONV_DIM * CONV_K * 2
+    io_bytes = L * (n * CONV_DIM * 2 + 2 * n * HV * D * 2 + 2 * n * HV * 2 + CONV_DIM * CONV_K * 2)
+    total = state_bytes + conv_bytes + io_bytes
+    achieved = total / (us * 1e-6) / 1e9
+    del graph
+    return {"us_per_step": us_max, "layers": L, "slots": n, "graph": True,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                         "frac": achieved / hbm_peak, "peak_source": peak_src,
+                         "algorithmic_bytes_per_step": total,
+                         "traffic": load_traffic().get("gdn_decode_step")},
+            "gpu_launches": args.steps * L * 2}
+
+
+def main():
+    args = parse()
+    if args.warmup < 3:
+        print("warning: fewer than 3 warm-up steps", file=sys.stderr)
+    world, rank, local = dist_setup(args)
+    try:
+        if args.impl == "reference":
+            run_reference(args, world, rank)
+        else:
+            run_ours(args, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

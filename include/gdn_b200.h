@@ -1,0 +1,180 @@
+/*
+ * gdn_b200.h -- C ABI of the B200 (sm_100a) GatedDeltaNet hot-path library.
+ *
+ * Every entry point takes plain device pointers, element counts and strides
+ * (in ELEMENTS, not bytes) and a cudaStream_t passed as void*.  Nothing here
+ * allocates device memory; callers own every buffer, so each call can be
+ * captured in a CUDA graph.  Calls are asynchronous on `stream` and return a
+ * gdn_status; on failure gdn_last_error() gives a message (thread-local).
+ *
+ * dtype codes: GDN_F32 = 0, GDN_BF16 = 1.  Unless stated otherwise `dtype`
+ * is the type of the activations (q, k, v, x, gate, out, conv state and
+ * conv/norm weights); g (log-decay), beta (given as float32, the reference
+ * upcasts it before use), recurrent states and A_log / dt_bias are always
+ * float32.
+ *
+ * Slot indexing: pools are [n_slots, ...] arrays; `slot_idx[b]` names the row
+ * of the pool that sequence b reads and writes.  A NULL slot_idx means the
+ * identity (b -> b).  Slot indices within one call must be distinct and in
+ * [0, n_slots); kernels skip out-of-range indices and set *err_flag (when
+ * given) to 1 instead of touching memory outside the pool.
+ *
+ * Each entry point names the reference interface it replaces (paths inside
+ * the reference project; "transformers" is models/qwen3_5/modeling_qwen3_5.py
+ * of transformers 5.5.x, which the reference patches).
+ */
+#ifndef GDN_B200_H
+#define GDN_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define GDN_API __attribute__((visibility("default")))
+#else
+#define GDN_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum gdn_status {
+  GDN_OK = 0,
+  GDN_ERR_ARG = 1,      /* null pointer, negative size, bad enum */
+  GDN_ERR_SHAPE = 2,    /* head dims / ratios this library does not build */
+  GDN_ERR_DTYPE = 3,    /* dtype code not supported for this entry point */
+  GDN_ERR_CUDA = 4,     /* a CUDA launch or attribute call failed */
+  GDN_ERR_WORKSPACE = 5 /* workspace missing or too small */
+};
+
+enum gdn_dtype { GDN_F32 = 0, GDN_BF16 = 1 };
+
+/* Conv rounding modes (both are the reference's code paths):
+ *   GDN_CONV_HF   : fp32 accumulation of the K taps (+bias), one rounding, as
+ *                   F.conv1d inside torch_causal_conv1d_update (transformers :210-226)
+ *   GDN_CONV_ELEM : products rounded to dtype, fp32 sum rounded, bias added in
+ *                   dtype, as elem_conv_update (src/cb_engine.py:43-51)      */
+enum gdn_conv_mode { GDN_CONV_HF = 0, GDN_CONV_ELEM = 1 };
+
+/* Message of the last failing call on this thread ("" if none). */
+GDN_API const char* gdn_last_error(void);
+
+/* Library version (major*10000 + minor*100 + patch). */
+GDN_API int gdn_version(void);
+
+/* ---------------------------------------------------------------------------
+ * a4. Gated RMSNorm.  Replaces Qwen3_5RMSNormGated.forward (transformers :181-191) and
+ * the reference's fused_gated_rmsnorm (src/cb_engine.py:65-67):
+ *   y = rnd(w * rnd(x * rsqrt(mean(x^2) + eps))) * silu(float(gate))
+ * x, gate, y: [rows, dim] with row strides x_rs, g_rs, y_rs; w: [dim] (dtype).
+ * dim <= 1024 and dim % 4 == 0.
+ */
+GDN_API int gdn_gated_rmsnorm(const void* x, int64_t x_rs, const void* gate, int64_t g_rs,
+                      const void* weight, void* y, int64_t y_rs, int64_t rows, int dim,
+                      float eps, int dtype, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * a3. Decode causal depthwise conv with conv-state update.  Replaces
+ * elem_conv_update (src/cb_engine.py:43-51) and torch_causal_conv1d_update
+ * (transformers :210-226), slot-indexed (src/cb_engine.py:325-328 passes the whole pool).
+ *   x: [B, C, T] at x[b*xs_b + c*xs_c + t*xs_t];  y likewise with ys_*.
+ *   conv_pool: [n_slots, C, K] contiguous, updated IN PLACE for rows slot_idx[b].
+ *   weight: [C, K]; bias: [C] or NULL; activation: 0 none, 1 silu.
+ *   K <= 8, T >= 1.
+ */
+GDN_API int gdn_conv_update(const void* x, int64_t xs_b, int64_t xs_c, int64_t xs_t, void* conv_pool,
+                    const int32_t* slot_idx, int64_t n_slots, const void* weight, const void* bias,
+                    void* y, int64_t ys_b, int64_t ys_c, int64_t ys_t, int B, int C, int T, int K,
+                    int activation, int mode, int dtype, int32_t* err_flag, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Prefill causal conv over packed varlen tokens, with conv-state carry and
+ * slot scatter.  Replaces the prefill conv of Qwen3_5GatedDeltaNet.forward
+ * (transformers :463-474) and of TPEngine.prefill / prefill_chunk (src/cb_tp.py:158-164,
+ * :236-244, :260).
+ *   x, y: [T_total, C] with token strides xs_t, ys_t (channel stride 1).
+ *   cu_seqlens: device int32 [B+1].
+ *   conv_pool: [n_slots, C, K]; sequence b starts from conv_pool[slot_idx[b]]
+ *   when use_initial != NULL && use_initial[b] != 0 (else zeros), and its
+ *   last K inputs are written back to conv_pool[slot_idx[b]].
+ *   conv_pool may be NULL (no state read or write).
+ */
+GDN_API int gdn_prefill_conv(const void* x, int64_t xs_t, void* y, int64_t ys_t, const int32_t* cu_seqlens,
+                     int B, void* conv_pool, const int32_t* slot_idx, const int32_t* use_initial,
+                     int64_t n_slots, const void* weight, const void* bias, int C, int K,
+                     int activation, int dtype, int32_t* err_flag, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * a2. Gated delta rule, token by token (decode).  Replaces
+ * recurrent_single_step (src/recurrent_single_step.py:8-32) and its T>1
+ * fallback torch_recurrent_gated_delta_rule (transformers :314-353).
+ *   q, k: [B, T, Hk, dk] at q[b*q_sb + t*q_st + h*dk + i] (likewise k);
+ *   v:    [B, T, Hv, dv] at v[b*v_sb + t*v_st + h*dv + i];
+ *   g, beta (both f32): [B, T, Hv] at g[b*gb_sb + t*gb_st + h];
+ *   out:  [B, T, Hv, dv] at out[b*o_sb + t*o_st + h*dv + i].
+ *   v-head h reads q/k head h / (Hv / Hk)  (repeat_interleave semantics).
+ *   init_pool [.., Hv, dk, dv] f32 read at init_slot[b] (NULL pool: zeros);
+ *   final_pool written at final_slot[b] (NULL pool: not written).  The two
+ *   may be the same pool (in-place slot update).
+ *   (dk, dv) in {(64,64), (128,128)}; Hv % Hk == 0.
+ */
+GDN_API int gdn_recurrent(const void* q, int64_t q_sb, int64_t q_st, const void* k, int64_t k_sb,
+                  int64_t k_st, const void* v, int64_t v_sb, int64_t v_st, const float* g,
+                  const float* beta, int64_t gb_sb, int64_t gb_st, const float* init_pool,
+                  const int32_t* init_slot, float* final_pool, const int32_t* final_slot,
+                  int64_t n_slots, void* out, int64_t o_sb, int64_t o_st, int B, int T, int Hk,
+                  int Hv, int dk, int dv, int use_qk_l2norm, int dtype, int32_t* err_flag,
+                  void* stream);
+
+/* ---------------------------------------------------------------------------
+ * a5+a3+a2+a4. One fused GDN decode layer for n slots (one token each), the
+ * operator part of CBEngine._gdn (src/cb_engine.py:318-352) between the input
+ * projections and out_proj:
+ *   conv update of mixed_qkv [n, C] (C = 2*Hk*dk + Hv*dv) with the slot's conv
+ *   state -> split q|k|v -> beta = sigmoid(b), g = -exp(A_log)*softplus(a+dt_bias)
+ *   -> l2norm(q), l2norm(k) -> single-step recurrence on rec_pool[slot_idx]
+ *   (in place) -> gated RMSNorm with gate z [n, Hv, dv] -> out [n, Hv, dv].
+ *   a, b: [n, Hv] (dtype); A_log, dt_bias: [Hv] f32; norm_w: [dv] (dtype).
+ * Needs a workspace of gdn_decode_layer_workspace_size() bytes (device).
+ */
+GDN_API size_t gdn_decode_layer_workspace_size(int n, int Hk, int Hv, int dk, int dv, int dtype);
+
+GDN_API int gdn_decode_layer(const void* mixed_qkv, int64_t mixed_rs, const void* z, const void* a,
+                     const void* b, const float* A_log, const float* dt_bias, const void* conv_w,
+                     const void* conv_b, void* conv_pool, float* rec_pool,
+                     const int32_t* slot_idx, int64_t n_slots, const void* norm_w, float eps,
+                     void* out, int n, int Hk, int Hv, int dk, int dv, int K, int conv_mode,
+                     void* workspace, size_t workspace_bytes, int dtype, int32_t* err_flag,
+                     void* stream);
+
+/* ---------------------------------------------------------------------------
+ * a1. Chunked gated delta rule (chunk 64) over packed varlen sequences.
+ * Replaces fast_chunk_gated_delta_rule_v2 (src/gdn_chunk_fast2.py:11-62),
+ * fast_chunk_gated_delta_rule (src/gdn_chunk_fast.py:65-142) and
+ * torch_chunk_gated_delta_rule (transformers :234-311); slot-indexed state read/write
+ * replaces the slot copies of src/cb_tp.py:179-180 and :256-261.
+ *   q, k: [T_total, Hk, dk] with token strides q_st, k_st; v: [T_total, Hv, dv]
+ *   with token stride v_st; g, beta (both f32): [T_total, Hv] token stride
+ *   gb_st; out: [T_total, Hv, dv] with token stride o_st.
+ *   cu_seqlens: device int32 [B+1].
+ *   Sequence b starts from init_pool[init_slot[b]] when init_pool != NULL and
+ *   (use_initial == NULL || use_initial[b]); otherwise from zeros.  Its final
+ *   state goes to final_pool[final_slot[b]] when final_pool != NULL.
+ *   (dk, dv) in {(64,64), (128,128)}; Hv % Hk == 0.
+ * GDN_BF16 runs on the tensor cores (bf16 operands, fp32 accumulation and
+ * fp32 state); GDN_F32 runs an fp32 CUDA-core path.
+ */
+GDN_API int gdn_chunk_prefill(const void* q, int64_t q_st, const void* k, int64_t k_st, const void* v,
+                      int64_t v_st, const float* g, const float* beta, int64_t gb_st,
+                      const int32_t* cu_seqlens, int B, int64_t T_total, const float* init_pool,
+                      const int32_t* init_slot, const int32_t* use_initial, float* final_pool,
+                      const int32_t* final_slot, int64_t n_slots, void* out, int64_t o_st, int Hk,
+                      int Hv, int dk, int dv, int use_qk_l2norm, int dtype, int32_t* err_flag,
+                      void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GDN_B200_H */

@@ -39,9 +39,11 @@ F32 = np.float32
 def bf16(x):
     """Round float32 values to the nearest bfloat16 (ties to even); returns float32."""
     x = np.ascontiguousarray(x, dtype=F32)
-    u = x.view(np.uint32).astype(np.uint64)
-    r = ((u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000).astype(np.uint32).view(F32)
-    return np.where(np.isnan(x), F32(np.nan), r).astype(F32)
+    u = x.view(np.uint32)
+    # finite values and infinities cannot carry past bit 31; NaNs are restored below
+    r = ((u + np.uint32(0x7FFF) + ((u >> np.uint32(16)) & np.uint32(1))) & np.uint32(0xFFFF0000)).view(F32)
+    nan = np.isnan(x)
+    return np.where(nan, F32(np.nan), r) if nan.any() else r
 
 
 def rnd(x, dt):

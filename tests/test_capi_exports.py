@@ -1,0 +1,75 @@
+"""The C-ABI library loads without a GPU and exports exactly what include/gdn_b200.h declares.
+
+No compute is launched here: the only calls made are ones the library rejects during argument
+validation, before any CUDA API call.
+"""
+import ctypes
+import os
+import re
+
+import pytest
+
+from conftest import ROOT, pkg
+
+HEADER = os.path.join(ROOT, "include", "gdn_b200.h")
+
+
+def declared_functions():
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    out = {}
+    for m in re.finditer(r"(?:^|\n)\s*(?:GDN_API\s+)?(?:const\s+)?(\w+\s*\*?)\s+(gdn_\w+)\s*\(([^)]*)\)\s*;", src):
+        params = [p.strip() for p in m.group(3).split(",") if p.strip() and p.strip() != "void"]
+        out[m.group(2)] = len(params)
+    return out
+
+
+@pytest.fixture(scope="module")
+def lib():
+    L = pkg("_lib")
+    if not os.path.exists(L.LIB_PATH):
+        pytest.fail("libgdn_b200.so is not built (run __graft_entry__.build())")
+    return L.load()
+
+
+def test_header_parses():
+    fns = declared_functions()
+    assert "gdn_chunk_prefill" in fns and "gdn_decode_layer" in fns and len(fns) >= 9
+
+
+def test_every_declared_symbol_is_exported_and_bound(lib):
+    L = pkg("_lib")
+    for name, nparams in declared_functions().items():
+        assert hasattr(lib, name), f"{name} not exported"
+        assert name in L.SIGNATURES, f"{name} has no ctypes signature"
+        assert len(L.SIGNATURES[name][1]) == nparams, f"{name}: {nparams} params in header"
+
+
+def test_no_undeclared_exports(lib):
+    # every bound signature corresponds to a header declaration
+    L = pkg("_lib")
+    assert set(L.SIGNATURES) == set(declared_functions())
+
+
+def test_validation_errors_without_gpu(lib):
+    L = pkg("_lib")
+    assert lib.gdn_version() >= 100
+    rc = lib.gdn_gated_rmsnorm(None, 0, None, 0, None, None, 0, -1, 128, 1e-6, 1, None)
+    assert rc == 1 and b"rows" in lib.gdn_last_error()
+    rc = lib.gdn_chunk_prefill(None, 0, None, 0, None, 0, None, None, 0, None, 1, 10, None, None, None, None,
+                               None, 0, None, 0, 16, 48, 128, 128, 1, 1, None, None)
+    assert rc == 1 and b"null" in lib.gdn_last_error()
+    rc = lib.gdn_recurrent(*([None, 0, 0] * 3), None, None, 0, 0, None, None, None, None, 0, None, 0, 0,
+                           1, 1, 16, 40, 128, 128, 1, 1, None, None)
+    assert rc == 2 and b"multiple" in lib.gdn_last_error()
+    with pytest.raises(RuntimeError, match="status 2"):
+        L.check(2, "probe")
+    assert lib.gdn_decode_layer_workspace_size(16, 16, 48, 128, 128, 1) >= 16 * 10240 * 2
+
+
+def test_ops_refuse_cpu_tensors():
+    import torch
+    ops = pkg("ops")
+    x = torch.zeros(4, 128, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        ops.gated_rmsnorm(x, x, torch.ones(128, dtype=torch.bfloat16))
