@@ -30,5 +30,6 @@ struct ChunkParams {
 };
 
 int run_chunk_simt(const ChunkParams& p, int D, int dtype, cudaStream_t s);
+int run_chunk_tc(const ChunkParams& p, int64_t T_total, cudaStream_t s);
 
 }  // namespace gdn

@@ -1,10 +1,6 @@
 // C entry point of the chunked prefill: argument checks and kernel selection.
 #include "chunk.cuh"
 
-namespace gdn {
-int run_chunk_simt(const ChunkParams& p, int D, int dtype, cudaStream_t s);
-}  // namespace gdn
-
 extern "C" int gdn_chunk_prefill(const void* q, int64_t q_st, const void* k, int64_t k_st, const void* v,
                                  int64_t v_st, const float* g, const float* beta, int64_t gb_st,
                                  const int32_t* cu_seqlens, int B, int64_t T_total, const float* init_pool,
@@ -31,5 +27,7 @@ extern "C" int gdn_chunk_prefill(const void* q, int64_t q_st, const void* k, int
   p.init_pool = init_pool; p.init_slot = init_slot; p.use_init = use_initial;
   p.final_pool = final_pool; p.final_slot = final_slot; p.n_slots = n_slots;
   p.out = out; p.o_st = o_st; p.B = B; p.Hk = Hk; p.Hv = Hv; p.l2norm = use_qk_l2norm; p.err = err_flag;
+  // bf16 activations at dk = dv = 128 run on the tensor cores; fp32 (and d = 64) on the CUDA cores
+  if (dtype == GDN_BF16 && dk == 128) return run_chunk_tc(p, T_total, as_stream(stream));
   return run_chunk_simt(p, dk, dtype, as_stream(stream));
 }

@@ -1,0 +1,704 @@
+// a1, tensor-core path.  Chunked gated delta rule (chunk 64, dk = dv = 128, bf16 activations,
+// fp32 state) on the 5th-generation tensor cores of sm_100a.
+//
+// One CTA (two warpgroups) per (sequence, value head); the fp32 state S [dk][dv] lives in TMEM for
+// the whole sequence.  The chunk algebra of fast_chunk_gated_delta_rule_v2
+// (src/gdn_chunk_fast2.py:37-59) is split into the part that does not depend on S and the part
+// that does, and the two run as a software pipeline on separate warpgroups:
+//
+//   intra-chunk warpgroup (warps 0-3), chunk j:
+//       TMA loads of raw q, k (un-repeated k-head) and v tiles (128-byte swizzle; never multicast)
+//       P1  [Q;K] [Q;K]^T  -> QK^T, KK^T and, on the diagonal, the squared row norms that give the
+//                             l2-norm factors rq, rk (rounded in bf16 as src/gdn_chunk_fast.py:17-18)
+//       CUDA cores: X = -(beta k k^T . decay) strictly lower; T = (I - X)^-1 by the blocked
+//                   inverse of src/gdn_chunk_fast.py:21-62; QKm = (q k^T . decay) causal
+//       P2  U^T = V^T (T diag beta)^T          P3  W^T = K^T (T diag(beta e^gc rk))^T
+//   recurrence warpgroup (warps 4-7), chunk j-1 (or j once the intra group hands it over):
+//       P4  vn^T = U^T - S^T W^T                (a-negated accumulate onto U^T)
+//       P5  o^T  = (S^T Q^T) . (rq scale e^gc) + vn^T QKm^T    (two accumulators)
+//       P6  S    = S e^gl + K^T (vn . rk e^(gl-gc))            (S pre-scaled when read)
+//       output through shared memory (a TMA store for full chunks), final S to the slot's pool row
+//
+// Hand-over uses mbarriers ("chunk ready" / "buffers freed"); per-chunk TMEM accumulators, the QKm
+// tile and the per-chunk vectors are double buffered so the intra group can run a chunk ahead.
+// All MMAs are M = 128 tcgen05.mma.kind::f16 (bf16 operands, fp32 accumulation); the state itself
+// is never rounded.  Tokens past the end of the sequence are zeroed in shared memory and get
+// beta = 0 and rq = rk = 0, which is what the reference's zero padding does.
+#include "chunk.cuh"
+#include "sm100.cuh"
+
+namespace gdn {
+namespace tcchunk {
+
+using namespace sm100;
+
+constexpr int kC = 64;
+constexpr int kD = 128;
+constexpr int kNT = 256;
+
+constexpr uint32_t TMEM_COLS = 512;
+constexpr int LT = 68;   // row stride (floats) of the fp32 64x64 scratch: 16-byte aligned rows
+constexpr int LP = 36;   // row stride of the 32x32 merge scratch
+constexpr float kLog2e = 1.4426950408889634f;
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+__device__ __forceinline__ uint32_t pack2(float a, float b) {
+  __nv_bfloat162 t = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&t);
+}
+
+__device__ __forceinline__ void unpack8(const uint4& u, float* x) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    x[2 * i] = __uint_as_float(w[i] << 16);
+    x[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+  }
+}
+
+// Store 32 fp32 values (scaled by f[j]) as 4 bf16 chunks of row r, chunks cc0..cc0+3.
+__device__ __forceinline__ void store_row32(uint8_t* tile, int R, int r, int cc0, const float* v) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint4 u;
+    u.x = pack2(v[8 * q + 0], v[8 * q + 1]);
+    u.y = pack2(v[8 * q + 2], v[8 * q + 3]);
+    u.z = pack2(v[8 * q + 4], v[8 * q + 5]);
+    u.w = pack2(v[8 * q + 6], v[8 * q + 7]);
+    *reinterpret_cast<uint4*>(tile + chunk_off(r, cc0 + q, R)) = u;
+  }
+}
+
+__device__ __forceinline__ float4 lds4(const float* p) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(smem_u32(p)));
+  return v;
+}
+__device__ __forceinline__ float lds1(const float* p) {
+  float v;
+  asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(smem_u32(p)));
+  return v;
+}
+__device__ __forceinline__ float f4get(const float4& v, int i) {
+  return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
+}
+// Barrier over one 128-thread warpgroup (ids 1 and 2; id 0 is __syncthreads).
+__device__ __forceinline__ void group_sync(int id) { asm volatile("bar.sync %0, 128;" ::"r"(id) : "memory"); }
+
+// T = (I - X)^-1 for the strictly lower 64x64 X held in fp32 shared memory (row stride LT), in
+// place, by the blocked scheme of src/gdn_chunk_fast.py:33-62: 16x16 diagonal blocks by the row
+// recurrence (evaluated column-wise), then pairwise merges T21 = (B X21) A.  Run by one warpgroup
+// (4 warps, `gid` its named barrier); P is 32 x LP floats of scratch.  In the merges a lane owns
+// one output column: the column operand is one conflict-free 32-bit load per row and the row
+// operand a uniform-address float4, which keeps the shared-memory wavefront count low.
+__device__ __forceinline__ void tri_inverse64(float* X, float* P, int warp, int lane, int gid) {
+  {  // diagonal block `warp`; lane j < 16 owns column j
+    const int b0 = 16 * warp, j = lane & 15;
+    float acc[16], r[16];
+    float4 xr[16][4];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) acc[i] = lds1(X + (b0 + i) * LT + b0 + j);
+#pragma unroll
+    for (int i = 0; i < 16; ++i)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) xr[i][q] = lds4(X + (b0 + i) * LT + b0 + 4 * q);
+#pragma unroll
+    for (int m = 0; m < 16; ++m) {
+      r[m] = m > j ? acc[m] : 0.f;
+#pragma unroll
+      for (int i = m + 1; i < 16; ++i) acc[i] = fmaf(f4get(xr[i][m >> 2], m & 3), r[m], acc[i]);
+    }
+    __syncwarp();
+    if (lane < 16) {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) X[(b0 + i) * LT + b0 + j] = i == j ? 1.f : (i > j ? r[i] : 0.f);
+    }
+  }
+  group_sync(gid);
+  {  // level 1: merge m = lane / 16 (blocks (0,1) or (2,3)), column c = lane % 16, rows 4w..4w+3
+    const int m = lane >> 4, c = lane & 15, lo = m * 32, hi = lo + 16, r0 = 4 * warp;
+    float a[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int tq = 0; tq < 4; ++tq) {
+      float x[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) x[u] = lds1(X + (hi + 4 * tq + u) * LT + lo + c);
+#pragma unroll
+      for (int rr = 0; rr < 4; ++rr) {
+        const float4 bv = lds4(X + (hi + r0 + rr) * LT + hi + 4 * tq);
+        a[rr] = fmaf(bv.w, x[3], fmaf(bv.z, x[2], fmaf(bv.y, x[1], fmaf(bv.x, x[0], a[rr]))));
+      }
+    }
+#pragma unroll
+    for (int rr = 0; rr < 4; ++rr) P[m * 16 * LP + (r0 + rr) * LP + c] = a[rr];
+    group_sync(gid);
+#pragma unroll
+    for (int rr = 0; rr < 4; ++rr) a[rr] = 0.f;
+#pragma unroll
+    for (int tq = 0; tq < 4; ++tq) {
+      float x[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) x[u] = lds1(X + (lo + 4 * tq + u) * LT + lo + c);
+#pragma unroll
+      for (int rr = 0; rr < 4; ++rr) {
+        const float4 pv = lds4(P + m * 16 * LP + (r0 + rr) * LP + 4 * tq);
+        a[rr] = fmaf(pv.w, x[3], fmaf(pv.z, x[2], fmaf(pv.y, x[1], fmaf(pv.x, x[0], a[rr]))));
+      }
+    }
+#pragma unroll
+    for (int rr = 0; rr < 4; ++rr) X[(hi + r0 + rr) * LT + lo + c] = a[rr];
+    group_sync(gid);
+  }
+  {  // level 2: column c = lane, rows 8w .. 8w+7
+    const int c = lane, r0 = 8 * warp;
+    float a[8];
+#pragma unroll
+    for (int rr = 0; rr < 8; ++rr) a[rr] = 0.f;
+#pragma unroll
+    for (int tq = 0; tq < 8; ++tq) {
+      float x[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) x[u] = lds1(X + (32 + 4 * tq + u) * LT + c);
+#pragma unroll
+      for (int rr = 0; rr < 8; ++rr) {
+        const float4 bv = lds4(X + (32 + r0 + rr) * LT + 32 + 4 * tq);
+        a[rr] = fmaf(bv.w, x[3], fmaf(bv.z, x[2], fmaf(bv.y, x[1], fmaf(bv.x, x[0], a[rr]))));
+      }
+    }
+#pragma unroll
+    for (int rr = 0; rr < 8; ++rr) P[(r0 + rr) * LP + c] = a[rr];
+    group_sync(gid);
+#pragma unroll
+    for (int rr = 0; rr < 8; ++rr) a[rr] = 0.f;
+#pragma unroll
+    for (int tq = 0; tq < 8; ++tq) {
+      float x[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) x[u] = lds1(X + (4 * tq + u) * LT + c);
+#pragma unroll
+      for (int rr = 0; rr < 8; ++rr) {
+        const float4 pv = lds4(P + (r0 + rr) * LP + 4 * tq);
+        a[rr] = fmaf(pv.w, x[3], fmaf(pv.z, x[2], fmaf(pv.y, x[1], fmaf(pv.x, x[0], a[rr]))));
+      }
+    }
+#pragma unroll
+    for (int rr = 0; rr < 8; ++rr) X[(32 + r0 + rr) * LT + c] = a[rr];
+    group_sync(gid);
+  }
+}
+
+// Per-chunk vectors handed from the intra warpgroup to the recurrence warpgroup (double buffered).
+struct ChunkVec {
+  float gc[64];   // log2-scaled cumulative decay
+  float bt[64];   // beta (0 past the sequence end)
+  float rn[128];  // l2norm factors: rq rows 0-63, rk rows 64-127 (0 past the end)
+  float egc[64];  // exp(gc)
+  float dkd[64];  // rk exp(gl - gc)
+  float bwc[64];  // beta exp(gc) rk
+  float gl, Gl;   // log2-scaled total decay of the chunk and exp of it
+  int nt;         // live tokens in the chunk
+  int pad;
+};
+
+// shared-memory map of the warp-specialised kernel (bytes from a 1024-byte aligned base)
+constexpr uint32_t W_QK0 = 0;          // QK stage 0: [Q d0-63 | K d0-63 | Q d64-127 | K d64-127]
+constexpr uint32_t W_QK1 = 32768;      // QK stage 1
+constexpr uint32_t W_V = 65536;        // V [s][v] (single buffer; intra group only)
+constexpr uint32_t W_S16 = 81920;      // S bf16 [k][v] (recurrence group)
+constexpr uint32_t W_WT = 114688;      // W^T [k][t]; then the output staging o [t][v]
+constexpr uint32_t W_VNT = 131072;     // vn^T [v][s]
+constexpr uint32_t W_VND = 147456;     // (vn . d)^T [v][s]
+constexpr uint32_t W_BU = 163840;      // T diag(beta) [t][s]
+constexpr uint32_t W_BW = 172032;      // T diag(beta e^gc rk) [t][s]
+constexpr uint32_t W_BQK0 = 180224;    // QKm [t][s], buffer 0
+constexpr uint32_t W_BQK1 = 188416;    // buffer 1
+constexpr uint32_t W_X = 196608;       // fp32 64 x LT inverse scratch (17408 B) + 32 x LP merge scratch
+constexpr uint32_t W_VEC = 218624;     // 2 x ChunkVec
+constexpr uint32_t W_BAR = W_VEC + 2 * 2048;  // mbarriers
+constexpr uint32_t W_SMEM = W_BAR + 128 + 1024;
+static_assert(sizeof(ChunkVec) <= 2048, "ChunkVec");
+static_assert(W_X + 64 * LT * 4 + 32 * LP * 4 <= W_VEC, "scratch");
+
+// TMEM columns
+constexpr uint32_t T_S = 0;      // state, 128 columns
+constexpr uint32_t T_P1 = 128;   // [Q;K][Q;K]^T, 128 columns (intra group)
+constexpr uint32_t T_U0 = 256;   // U^T -> vn^T -> vn^T QKm^T, 64 columns per buffer
+constexpr uint32_t T_W0 = 384;   // W^T -> S^T Q^T, 64 columns per buffer
+
+__global__ void __launch_bounds__(kNT, 1)
+    chunk_tc_kernel(const ChunkParams p, const __grid_constant__ CUtensorMap tq,
+                    const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
+                    const __grid_constant__ CUtensorMap to, const int use_tma_store) {
+  extern __shared__ __align__(1024) uint8_t smraw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smraw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sb = smem_u32(sm);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + W_BAR);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + W_BAR + 96);
+  float* Xs = reinterpret_cast<float*>(sm + W_X);
+  float* Ps = Xs + 64 * LT;
+  // mbarriers: 0,1 QK stage full; 2 V full; 3 intra MMA; 4 recurrence MMA; 5,6 chunk ready; 7,8 buffers freed
+  const uint32_t bar_qk0 = smem_u32(&bars[0]), bar_v = smem_u32(&bars[2]);
+  const uint32_t bar_mi = smem_u32(&bars[3]), bar_mr = smem_u32(&bars[4]);
+  const uint32_t bar_ready0 = smem_u32(&bars[5]), bar_free0 = smem_u32(&bars[7]);
+
+  const int h = blockIdx.x, b = blockIdx.y;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int grp = warp >> 2;          // 0: intra-chunk group, 1: recurrence group
+  const int wg = warp & 3;            // warp within the group = TMEM lane quarter
+  const int row = 32 * wg + lane;     // TMEM lane of this thread
+  const uint32_t lane_off = uint32_t(32 * wg) << 16;
+  const int hk = h / (p.Hv / p.Hk);
+  const float scale = float(1.0 / sqrt(double(kD)));
+  const int64_t s0 = p.cu[b], s1 = p.cu[b + 1];
+
+  const bool want_init = p.init_pool && (p.use_init == nullptr || p.use_init[b] != 0);
+  const int64_t islot = p.init_slot ? int64_t(p.init_slot[b]) : int64_t(b);
+  const int64_t fslot = p.final_slot ? int64_t(p.final_slot[b]) : int64_t(b);
+  if ((want_init && (islot < 0 || islot >= p.n_slots)) || (p.final_pool && (fslot < 0 || fslot >= p.n_slots))) {
+    if (tid == 0 && p.err) atomicExch(p.err, 1);
+    return;
+  }
+  const int nchunks = int((s1 - s0 + kC - 1) / kC);
+
+  auto issue_qk = [&](int ci) {
+    const int st = ci & 1;
+    const uint32_t bar = bar_qk0 + 8 * st;
+    const uint32_t qk = sb + (st ? W_QK1 : W_QK0);
+    const int c0 = int(s0) + ci * kC;
+    mbar_expect_tx(bar, 4 * 8192);
+    tma_load_3d(qk + 0, &tq, bar, 0, hk, c0);
+    tma_load_3d(qk + 8192, &tk, bar, 0, hk, c0);
+    tma_load_3d(qk + 16384, &tq, bar, 64, hk, c0);
+    tma_load_3d(qk + 24576, &tk, bar, 64, hk, c0);
+  };
+  auto issue_v = [&](int ci) {
+    const int c0 = int(s0) + ci * kC;
+    mbar_expect_tx(bar_v, 2 * 8192);
+    tma_load_3d(sb + W_V, &tv, bar_v, 0, h, c0);
+    tma_load_3d(sb + W_V + 8192, &tv, bar_v, 64, h, c0);
+  };
+
+  if (tid == 0) {
+    for (int i = 0; i < 9; ++i) mbar_init(smem_u32(&bars[i]), 1);
+    fence_mbar_init();
+    prefetch_tmap(&tq);
+    prefetch_tmap(&tk);
+    prefetch_tmap(&tv);
+    if (nchunks > 0) {
+      issue_qk(0);
+      issue_v(0);
+    }
+    if (nchunks > 1) issue_qk(1);
+  }
+  if (warp == 0) {
+    tmem_alloc(smem_u32(tmem_slot), TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  bool ok = true;
+
+  if (grp == 0) {
+    // ======================================================================== intra-chunk group
+    uint32_t ph_mi = 0;
+    float pg0 = 0.f, pg1 = 0.f, pb0 = 0.f, pb1 = 0.f;
+    auto load_gates = [&](int ci) {
+      const int64_t c0 = s0 + int64_t(ci) * kC;
+      const int t0 = 2 * lane, t1 = 2 * lane + 1;
+      pg0 = c0 + t0 < s1 ? p.g[(c0 + t0) * p.gb_st + h] : 0.f;
+      pg1 = c0 + t1 < s1 ? p.g[(c0 + t1) * p.gb_st + h] : 0.f;
+      pb0 = c0 + t0 < s1 ? p.beta[(c0 + t0) * p.gb_st + h] : 0.f;
+      pb1 = c0 + t1 < s1 ? p.beta[(c0 + t1) * p.gb_st + h] : 0.f;
+    };
+    if (warp == 0 && nchunks > 0) load_gates(0);
+    for (int ci = 0; ci < nchunks; ++ci) {
+      const int bf = ci & 1;
+      ChunkVec& cv = *reinterpret_cast<ChunkVec*>(sm + W_VEC + 2048 * bf);
+      const int64_t c0 = s0 + int64_t(ci) * kC;
+      const int nt = int((s1 - c0) < kC ? (s1 - c0) : kC);
+      uint8_t* qk = sm + (bf ? W_QK1 : W_QK0);
+      const uint32_t qk_a = sb + (bf ? W_QK1 : W_QK0);
+      const uint32_t bqk = bf ? W_BQK1 : W_BQK0;
+      // chunk ci-2 has left this buffer set (vectors, QKm tile, TMEM U/W buffers)
+      if (ci >= 2 && ok && !mbar_wait(bar_free0 + 8 * bf, uint32_t((ci - 2) >> 1) & 1u)) ok = false;
+      tc_fence_after();
+      if (warp == 0) {  // gates: gc = cumsum(g) (log2-scaled), beta; prefetch the next chunk's
+        const int t0 = 2 * lane, t1 = 2 * lane + 1;
+        const float g0 = pg0 * kLog2e, g1 = pg1 * kLog2e;
+        cv.bt[t0] = pb0;
+        cv.bt[t1] = pb1;
+        float pre = g0 + g1;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const float nb = __shfl_up_sync(0xffffffffu, pre, o);
+          if (lane >= o) pre += nb;
+        }
+        const float ex = pre - (g0 + g1);
+        const float a0 = ex + g0, a1 = ex + g0 + g1;
+        cv.gc[t0] = a0;
+        cv.gc[t1] = a1;
+        cv.egc[t0] = ex2(a0);
+        cv.egc[t1] = ex2(a1);
+        const float gl = __shfl_sync(0xffffffffu, a1, 31);
+        if (lane == 0) {
+          cv.gl = gl;
+          cv.Gl = ex2(gl);
+          cv.nt = nt;
+        }
+        if (ci + 1 < nchunks) load_gates(ci + 1);
+      }
+      if (ok && !mbar_wait(bar_qk0 + 8 * bf, uint32_t(ci >> 1) & 1u)) ok = false;
+      if (nt < kC) {  // zero the q/k rows past the sequence end (they hold the next sequence)
+        for (int i = tid; i < (kC - nt) * 32; i += 128) {
+          const int r = nt + (i >> 5), tile = (i >> 3) & 3, cc = i & 7;
+          *reinterpret_cast<uint4*>(qk + tile * 8192 + chunk_off(r, cc, 128)) = make_uint4(0, 0, 0, 0);
+        }
+        fence_async_smem();
+      }
+      tc_fence_before();
+      group_sync(1);
+      if (tid == 0) {  // P1: [Q;K] [Q;K]^T
+        tc_fence_after();
+        const uint32_t id = make_idesc(128, 128, false, false);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          umma(tmem + T_P1, desc_kmajor(qk_a, 128, kk), desc_kmajor(qk_a, 128, kk), id, kk > 0);
+        umma_commit(bar_mi);
+      }
+      if (ok && !mbar_wait(bar_mi, ph_mi)) ok = false;
+      ph_mi ^= 1u;
+      tc_fence_after();
+      {  // l2-norm factors from the diagonal (bf16 arithmetic as the reference's l2norm)
+        float dg[32];
+        tmem_ld32(tmem + T_P1 + lane_off + 32 * wg, dg);
+        float ss = dg[0];
+#pragma unroll
+        for (int j = 1; j < 32; ++j) ss = j == lane ? dg[j] : ss;
+        float inv = 1.f;
+        if (p.l2norm) inv = bf16r(1.0f / sqrtf(bf16r(bf16r(ss) + 1e-6f)));
+        cv.rn[row] = (row & 63) < nt ? inv : 0.f;
+      }
+      group_sync(1);
+      if (tid < 64) {
+        const float rk = cv.rn[64 + tid];
+        cv.dkd[tid] = rk * ex2(cv.gl - cv.gc[tid]);
+        cv.bwc[tid] = cv.bt[tid] * cv.egc[tid] * rk;
+      }
+      {  // P1 epilogue: QKm tile (rows 0-63) and X (rows 64-127), from the K columns 64-127
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          float a[32];
+          tmem_ld32(tmem + T_P1 + lane_off + 64 + 32 * half, a);
+          if (row < 64) {
+            const int t = row;
+            const float gt = cv.gc[t], f = cv.rn[t] * scale;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const int s = 32 * half + j;
+              a[j] = (s <= t) ? a[j] * f * cv.rn[64 + s] * ex2(gt - cv.gc[s]) : 0.f;
+            }
+            store_row32(sm + bqk, 64, t, 4 * half, a);
+          } else {
+            const int i = row - 64;
+            const float gi = cv.gc[i], f = cv.rn[64 + i] * cv.bt[i];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const int s = 32 * half + j;
+              Xs[i * LT + s] = (s < i) ? -(a[j] * f * cv.rn[64 + s]) * ex2(gi - cv.gc[s]) : 0.f;
+            }
+          }
+        }
+      }
+      group_sync(1);
+      tri_inverse64(Xs, Ps, wg, lane, 1);
+      {  // B_U = T diag(beta), B_W = T diag(beta e^gc rk): thread -> row t, 32 columns
+        const int t = tid >> 1, cb = (tid & 1) * 32;
+        float u[32], w[32];
+#pragma unroll
+        for (int e4 = 0; e4 < 8; ++e4) {
+          const float4 tv4 = lds4(Xs + t * LT + cb + 4 * e4);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int s = cb + 4 * e4 + e;
+            const float tv = f4get(tv4, e);
+            u[4 * e4 + e] = tv * cv.bt[s];
+            w[4 * e4 + e] = tv * cv.bwc[s];
+          }
+        }
+        store_row32(sm + W_BU, 64, t, cb >> 3, u);
+        store_row32(sm + W_BW, 64, t, cb >> 3, w);
+      }
+      if (ok && !mbar_wait(bar_v, uint32_t(ci) & 1u)) ok = false;
+      if (nt < kC) {
+        for (int i = tid; i < (kC - nt) * 16; i += 128) {
+          const int r = nt + (i >> 4), tile = (i >> 3) & 1, cc = i & 7;
+          *reinterpret_cast<uint4*>(sm + W_V + tile * 8192 + chunk_off(r, cc, 64)) = make_uint4(0, 0, 0, 0);
+        }
+      }
+      fence_async_smem();
+      tc_fence_before();
+      group_sync(1);
+      if (tid == 0) {  // P2: U^T = V^T B_U^T;  P3: W^T = K^T B_W^T
+        tc_fence_after();
+        const uint32_t id = make_idesc(128, 64, true, false);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          umma(tmem + T_U0 + 64 * bf, desc_mnmajor(sb + W_V, 64, kk), desc_kmajor(sb + W_BU, 64, kk), id, kk > 0);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          umma(tmem + T_W0 + 64 * bf, desc_mnmajor(qk_a + 8192, 128, kk), desc_kmajor(sb + W_BW, 64, kk), id,
+               kk > 0);
+        umma_commit(bar_mi);
+      }
+      if (ok && !mbar_wait(bar_mi, ph_mi)) ok = false;
+      ph_mi ^= 1u;
+      tc_fence_before();
+      group_sync(1);
+      if (tid == 0) {
+        if (ci + 1 < nchunks) {  // the V buffer is free: fetch the next chunk's
+          fence_async_smem();
+          issue_v(ci + 1);
+        }
+        mbar_arrive(bar_ready0 + 8 * bf);  // hand chunk ci to the recurrence group
+      }
+    }
+  } else {
+    // ======================================================================== recurrence group
+    const int rt = tid - 128;
+    uint32_t ph_mr = 0;
+    {  // initial state -> TMEM (thread: row k, all 128 columns)
+      float v[32];
+#pragma unroll
+      for (int part = 0; part < 4; ++part) {
+        if (want_init) {
+          const float4* src = reinterpret_cast<const float4*>(p.init_pool + (islot * p.Hv + h) * int64_t(kD * kD) +
+                                                              int64_t(row) * kD + 32 * part);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float4 f = src[i];
+            v[4 * i] = f.x; v[4 * i + 1] = f.y; v[4 * i + 2] = f.z; v[4 * i + 3] = f.w;
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = 0.f;
+        }
+        tmem_st32(tmem + T_S + lane_off + 32 * part, v);
+      }
+      tmem_st_wait();
+    }
+    for (int ci = 0; ci < nchunks; ++ci) {
+      const int bf = ci & 1;
+      const ChunkVec& cv = *reinterpret_cast<const ChunkVec*>(sm + W_VEC + 2048 * bf);
+      const int64_t c0 = s0 + int64_t(ci) * kC;
+      const uint32_t qk_a = sb + (bf ? W_QK1 : W_QK0);
+      const uint32_t bqk = bf ? W_BQK1 : W_BQK0;
+      const uint32_t tU = tmem + T_U0 + 64 * bf, tW = tmem + T_W0 + 64 * bf;
+      if (ok && !mbar_wait(bar_ready0 + 8 * bf, uint32_t(ci >> 1) & 1u)) ok = false;
+      tc_fence_after();
+      if (rt == 0) bulk_wait_read();  // the previous chunk's output store has left W_WT
+      group_sync(2);
+      const int nt = cv.nt;
+      {  // S -> bf16 tile (operand of P4/P5), S e^gl -> TMEM (P6 accumulates onto it); W^T tile
+        const float Gl = cv.Gl;
+#pragma unroll
+        for (int part = 0; part < 4; ++part) {
+          float sv[32];
+          tmem_ld32(tmem + T_S + lane_off + 32 * part, sv);
+          store_row32(sm + W_S16, 128, row, 4 * part, sv);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) sv[j] *= Gl;
+          tmem_st32(tmem + T_S + lane_off + 32 * part, sv);
+        }
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          float w[32];
+          tmem_ld32(tW + lane_off + 32 * half, w);
+          store_row32(sm + W_WT, 128, row, 4 * half, w);
+        }
+        tmem_st_wait();
+      }
+      fence_async_smem();
+      tc_fence_before();
+      group_sync(2);
+      if (rt == 0) {  // P4: vn^T = U^T - S^T W^T
+        tc_fence_after();
+        const uint32_t id = make_idesc(128, 64, true, true, true);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) umma(tU, desc_mnmajor(sb + W_S16, 128, kk), desc_mnmajor(sb + W_WT, 128, kk), id, 1);
+        umma_commit(bar_mr);
+      }
+      if (ok && !mbar_wait(bar_mr, ph_mr)) ok = false;
+      ph_mr ^= 1u;
+      tc_fence_after();
+      {  // vn^T tiles: plain (P5) and scaled by rk e^(gl-gc) (P6)
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          float a[32], d[32];
+          tmem_ld32(tU + lane_off + 32 * half, a);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) d[j] = a[j] * cv.dkd[32 * half + j];
+          store_row32(sm + W_VNT, 128, row, 4 * half, a);
+          store_row32(sm + W_VND, 128, row, 4 * half, d);
+        }
+      }
+      fence_async_smem();
+      tc_fence_before();
+      group_sync(2);
+      if (rt == 0) {  // P5: W = S^T Q^T, U = vn^T QKm^T;  P6: S += K^T (vn . d)
+        tc_fence_after();
+        const uint32_t ia = make_idesc(128, 64, true, false);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) umma(tW, desc_mnmajor(sb + W_S16, 128, kk), desc_kmajor(qk_a, 128, kk), ia, kk > 0);
+        const uint32_t ib = make_idesc(128, 64, false, false);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) umma(tU, desc_kmajor(sb + W_VNT, 128, kk), desc_kmajor(sb + bqk, 64, kk), ib, kk > 0);
+        const uint32_t ic = make_idesc(128, 128, true, false);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          umma(tmem + T_S, desc_mnmajor(qk_a + 8192, 128, kk), desc_kmajor(sb + W_VND, 128, kk), ic, 1);
+        umma_commit(bar_mr);
+      }
+      if (ok && !mbar_wait(bar_mr, ph_mr)) ok = false;
+      ph_mr ^= 1u;
+      tc_fence_after();
+      {  // output o[t][v] = rq_t scale e^gc_t (S^T q_t)[v] + (vn^T QKm^T)[v][t] -> staging (W_WT)
+        __nv_bfloat16* ot = reinterpret_cast<__nv_bfloat16*>(sm + W_WT);
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          float a[32], c[32];
+          tmem_ld32(tW + lane_off + 32 * half, a);
+          tmem_ld32(tU + lane_off + 32 * half, c);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int t = 32 * half + j;
+            ot[t * kD + row] = __float2bfloat16_rn(a[j] * (cv.rn[t] * scale * cv.egc[t]) + c[j]);
+          }
+        }
+      }
+      fence_async_smem();
+      tc_fence_before();
+      group_sync(2);
+      if (use_tma_store && nt == kC) {
+        if (rt == 0) {
+          tma_store_3d(&to, sb + W_WT, 0, h, int(c0));
+          bulk_commit();
+        }
+      } else {
+        const uint8_t* ot = sm + W_WT;
+        __nv_bfloat16* og = reinterpret_cast<__nv_bfloat16*>(p.out) + int64_t(h) * kD;
+#pragma unroll
+        for (int k8 = 0; k8 < 8; ++k8) {
+          const int cidx = rt + 128 * k8, t = cidx >> 4, cc = cidx & 15;
+          if (t < nt)
+            *reinterpret_cast<uint4*>(og + (c0 + t) * p.o_st + cc * 8) =
+                *reinterpret_cast<const uint4*>(ot + t * 256 + cc * 16);
+        }
+      }
+      group_sync(2);
+      if (rt == 0) {  // chunk ci is done with its buffer set: prefetch chunk ci+2 into it, free it
+        if (ci + 2 < nchunks) {
+          fence_async_smem();
+          issue_qk(ci + 2);
+        }
+        mbar_arrive(bar_free0 + 8 * bf);
+      }
+    }
+    // final state
+    if (p.final_pool) {
+#pragma unroll
+      for (int part = 0; part < 4; ++part) {
+        float v[32];
+        tmem_ld32(tmem + T_S + lane_off + 32 * part, v);
+        float4* dst = reinterpret_cast<float4*>(p.final_pool + (fslot * p.Hv + h) * int64_t(kD * kD) +
+                                                int64_t(row) * kD + 32 * part);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+      }
+    }
+    if (rt == 0) bulk_wait_all();
+  }
+  if (!ok && p.err) atomicExch(p.err, 2);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, TMEM_COLS);
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(f);
+  }
+  return fn;
+}
+
+// 3-D map over a [T, H, 128] bf16 tensor with token stride `tok_stride` elements; box = 64 dims x
+// 1 head x 64 tokens, 128-byte swizzle (the UMMA canonical layout), zero fill out of bounds.
+static int make_map(CUtensorMap* m, const void* base, int H, int64_t T, int64_t tok_stride, bool store = false) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(GDN_ERR_CUDA, "gdn_chunk_prefill: cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[3] = {cuuint64_t(kD), cuuint64_t(H), cuuint64_t(T)};
+  cuuint64_t strides[2] = {cuuint64_t(kD) * 2, cuuint64_t(tok_stride) * 2};
+  // loads: 64-element inner box with the 128-byte swizzle; the output store: a dense 128 x 64 box
+  cuuint32_t box[3] = {store ? 128u : 64u, 1, 64};
+  cuuint32_t es[3] = {1, 1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, es,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, store ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(GDN_ERR_CUDA, "gdn_chunk_prefill: tensor map encode failed (%d)", int(r));
+  return GDN_OK;
+}
+
+}  // namespace tcchunk
+
+int run_chunk_tc(const ChunkParams& p, int64_t T_total, cudaStream_t s) {
+  using namespace tcchunk;
+  const void* bases[3] = {p.q, p.k, p.v};
+  const int64_t strides[3] = {p.q_st, p.k_st, p.v_st};
+  for (int i = 0; i < 3; ++i) {
+    if (!aligned(bases[i], 16) || (strides[i] % 8) != 0)
+      return fail(GDN_ERR_ARG, "gdn_chunk_prefill: q/k/v need 16-byte aligned bases and token strides "
+                               "that are multiples of 8 elements");
+  }
+  if (T_total >= (int64_t(1) << 31)) return fail(GDN_ERR_ARG, "gdn_chunk_prefill: T_total too large");
+  CUtensorMap mq, mk, mv, mo;
+  int rc = make_map(&mq, p.q, p.Hk, T_total, p.q_st);
+  if (!rc) rc = make_map(&mk, p.k, p.Hk, T_total, p.k_st);
+  if (!rc) rc = make_map(&mv, p.v, p.Hv, T_total, p.v_st);
+  if (rc) return rc;
+  // full output chunks leave through a TMA store when the output rows allow one
+  int use_store = aligned(p.out, 16) && (p.o_st % 8) == 0 && T_total > 0;
+  if (use_store && make_map(&mo, p.out, p.Hv, T_total, p.o_st, true) != GDN_OK) use_store = 0;
+  if (!use_store) mo = mq;  // never read
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(chunk_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         int(W_SMEM));
+    if (e != cudaSuccess) return fail(GDN_ERR_CUDA, "chunk_tc: smem attribute: %s", cudaGetErrorString(e));
+    if (dev >= 0 && dev < 64) attr_set[dev] = true;
+  }
+  chunk_tc_kernel<<<dim3(p.Hv, p.B), kNT, W_SMEM, s>>>(p, mq, mk, mv, mo, use_store);
+  return check_launch("gdn_chunk_prefill (tensor cores)");
+}
+
+}  // namespace gdn

@@ -334,3 +334,45 @@ def test_decode_layer_matches_oracle_composition(ops):
     assert np.abs(N(rec_d)[slot] - rp[slot]).max() < 1e-4
     untouched = np.setdiff1d(np.arange(S), slot)
     assert np.array_equal(N(rec_d)[untouched], rec_pool[untouched])
+
+
+# ----------------------------------------------------------------------------- full config-1 size
+def _config1(seed=0):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    lens = torch.randint(200, 1201, (16,), generator=g).tolist()
+    Tt = sum(lens)
+    q = torch.randn(Tt, 16, 128, generator=g)
+    k = torch.randn(Tt, 16, 128, generator=g)
+    q = (q / q.norm(dim=-1, keepdim=True)).to(torch.bfloat16)
+    k = (k / k.norm(dim=-1, keepdim=True)).to(torch.bfloat16)
+    v = torch.randn(Tt, 48, 128, generator=g).to(torch.bfloat16)
+    beta = torch.sigmoid(torch.randn(Tt, 48, generator=g)).to(torch.bfloat16).float()
+    gg = (-(0.01 + 0.99 * torch.rand(Tt, 48, generator=g))).to(torch.bfloat16).float()
+    init = torch.randn(16, 48, 128, 128, generator=g) * 0.02
+    cu = torch.tensor([0] + np.cumsum(lens).tolist(), dtype=torch.int32)
+    return lens, q, k, v, gg, beta, init, cu
+
+
+def test_chunk_tc_full_config1_vs_oracle_and_fp32_path(ops):
+    """Config 1 at full size through the tensor-core kernel (bf16), checked (a) against the fp32
+    CUDA-core kernel on every token and head, and (b) against the CPU oracle on two sequences."""
+    lens, q, k, v, gg, beta, init, cu = _config1()
+    dq, dk_, dv_ = q.to(DEV), k.to(DEV), v.to(DEV)
+    dg, db, dcu = gg.to(DEV), beta.to(DEV), cu.to(DEV)
+    slot = torch.arange(16, dtype=torch.int32, device=DEV).flip(0).contiguous()
+    use = torch.ones(16, dtype=torch.int32, device=DEV)
+    pool_tc = init.to(DEV)[slot.long()].contiguous()          # slot s holds sequence 15-s's state
+    o_tc = ops.chunk_prefill_varlen(dq, dk_, dv_, dg, db, dcu, pool_tc, slot, use, True)
+    pool_32 = init.to(DEV)[slot.long()].contiguous()
+    o_32 = ops.chunk_prefill_varlen(dq.float(), dk_.float(), dv_.float(), dg, db, dcu, pool_32, slot, use, True)
+    torch.cuda.synchronize()
+    assert (o_tc.float() - o_32).abs().max().item() < 2e-2
+    assert (pool_tc - pool_32).abs().max().item() < 2e-2
+    for b in (0, 7):
+        s, e = int(cu[b]), int(cu[b + 1])
+        ro, rs = O.chunk_gated_delta_rule(O.repeat_heads(q[s:e].float().numpy(), 3)[None],
+                                          O.repeat_heads(k[s:e].float().numpy(), 3)[None],
+                                          v[s:e].float().numpy()[None], gg[s:e].numpy()[None],
+                                          beta[s:e].numpy()[None], 64, init[b].numpy()[None], True, True, "bf16")
+        assert bf16_ok(N(o_tc[s:e]), ro[0])
+        assert np.abs(N(pool_tc[15 - b]) - rs[0]).max() < 2e-2
