@@ -1,0 +1,76 @@
+// gdn_decode_layer_noalloc: the fused decode layer for callers that cannot allocate device memory.
+//
+// Some hosts of this library never let a plugin call cudaMalloc: a serving runtime that owns the
+// whole device-memory budget and hands plugins only the tensors they work on, or a latency-bound
+// decode loop where cudaMalloc's implicit device synchronisation is not acceptable.  Such a
+// caller still owns every input and output, but it has no way to provide the workspace that
+// gdn_decode_layer needs between its conv kernel and its recurrence kernel.  This entry point
+// takes that workspace from a fixed-size array in device memory that belongs to the library
+// instead.
+//
+// The array (kNoAllocScratchBytes) lives in every GPU that loads the library until the process
+// exits.  Its device address is looked up once per device, on the first call made with that
+// device current; make that first call before any stream capture.  All calls on a device share
+// the one array and it keeps whatever the last call left there: the conv kernel fully writes the
+// part a call uses before the recurrence kernel reads it, so nothing has to start at zero, but
+// two calls whose kernels overlap on the GPU (different streams, no ordering between them) race
+// on it.  Requests larger than the array are rejected with GDN_ERR_WORKSPACE; nothing here
+// calls cudaMalloc, cudaFree or any allocating library routine.
+#include <mutex>
+
+#include "common.cuh"
+
+namespace gdn {
+
+constexpr size_t kNoAllocScratchBytes = size_t(2) << 20;  // 2 MiB per GPU
+constexpr int kMaxDevices = 64;
+
+static __device__ __align__(256) unsigned char g_decode_scratch[kNoAllocScratchBytes];
+
+static std::mutex g_scratch_mu;
+static void* g_scratch_addr[kMaxDevices] = {};
+
+// Device address of g_decode_scratch on the current device (looked up once per device).
+static int scratch_address(void** out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(GDN_ERR_CUDA, "gdn_decode_layer_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices) return fail(GDN_ERR_ARG, "gdn_decode_layer_noalloc: device %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (!g_scratch_addr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_decode_scratch);
+    if (e != cudaSuccess || !p)
+      return fail(GDN_ERR_CUDA, "gdn_decode_layer_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+    g_scratch_addr[dev] = p;
+  }
+  *out = g_scratch_addr[dev];
+  return GDN_OK;
+}
+
+}  // namespace gdn
+
+extern "C" size_t gdn_decode_layer_noalloc_max_bytes(void) { return gdn::kNoAllocScratchBytes; }
+
+extern "C" int gdn_decode_layer_noalloc(const void* mixed_qkv, int64_t mixed_rs, const void* z, const void* a,
+                                        const void* b, const float* A_log, const float* dt_bias,
+                                        const void* conv_w, const void* conv_b, void* conv_pool, float* rec_pool,
+                                        const int32_t* slot_idx, int64_t n_slots, const void* norm_w, float eps,
+                                        void* out, int n, int Hk, int Hv, int dk, int dv, int K, int conv_mode,
+                                        int dtype, int32_t* err_flag, void* stream) {
+  using namespace gdn;
+  if (n < 0 || Hk <= 0 || Hv <= 0 || dk <= 0 || dv <= 0)
+    return fail(GDN_ERR_ARG, "gdn_decode_layer_noalloc: n=%d Hk=%d Hv=%d dk=%d dv=%d", n, Hk, Hv, dk, dv);
+  const size_t need = gdn_decode_layer_workspace_size(n, Hk, Hv, dk, dv, dtype);
+  if (need > kNoAllocScratchBytes)
+    return fail(GDN_ERR_WORKSPACE,
+                "gdn_decode_layer_noalloc: needs %zu bytes of scratch, the built-in array holds %zu "
+                "(n * (2*Hk*dk + Hv*dv) * element size must fit)",
+                need, kNoAllocScratchBytes);
+  void* scratch = nullptr;
+  int rc = scratch_address(&scratch);
+  if (rc) return rc;
+  return gdn_decode_layer(mixed_qkv, mixed_rs, z, a, b, A_log, dt_bias, conv_w, conv_b, conv_pool, rec_pool,
+                          slot_idx, n_slots, norm_w, eps, out, n, Hk, Hv, dk, dv, K, conv_mode, scratch,
+                          kNoAllocScratchBytes, dtype, err_flag, stream);
+}

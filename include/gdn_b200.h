@@ -149,6 +149,30 @@ GDN_API int gdn_decode_layer(const void* mixed_qkv, int64_t mixed_rs, const void
                      void* stream);
 
 /* ---------------------------------------------------------------------------
+ * gdn_decode_layer for callers that cannot allocate device memory.  This
+ * entry point has no counterpart in the reference; the reference never
+ * separates workspace from its torch ops.  Hosts such as a serving runtime
+ * that owns the whole device-memory budget, or a decode loop that cannot pay
+ * cudaMalloc's implicit synchronisation, pass only inputs and outputs here; the
+ * workspace is a fixed array of gdn_decode_layer_noalloc_max_bytes() (2 MiB)
+ * inside the library, held by every GPU that loads it until exit.  Its address
+ * is looked up on the first call per device (make that call before any stream
+ * capture).  All calls on a device share that array: calls whose kernels
+ * overlap on the GPU race.  Nothing in it has to start zeroed (each call
+ * writes the part it reads).  Requests larger than the array return
+ * GDN_ERR_WORKSPACE.  Arguments as gdn_decode_layer minus the workspace.
+ */
+GDN_API size_t gdn_decode_layer_noalloc_max_bytes(void);
+
+GDN_API int gdn_decode_layer_noalloc(const void* mixed_qkv, int64_t mixed_rs, const void* z, const void* a,
+                                     const void* b, const float* A_log, const float* dt_bias,
+                                     const void* conv_w, const void* conv_b, void* conv_pool,
+                                     float* rec_pool, const int32_t* slot_idx, int64_t n_slots,
+                                     const void* norm_w, float eps, void* out, int n, int Hk, int Hv,
+                                     int dk, int dv, int K, int conv_mode, int dtype,
+                                     int32_t* err_flag, void* stream);
+
+/* ---------------------------------------------------------------------------
  * a1. Chunked gated delta rule (chunk 64) over packed varlen sequences.
  * Replaces fast_chunk_gated_delta_rule_v2 (src/gdn_chunk_fast2.py:11-62),
  * fast_chunk_gated_delta_rule (src/gdn_chunk_fast.py:65-142) and
