@@ -34,7 +34,8 @@ using namespace sm100;
 
 constexpr int kC = 64;
 constexpr int kD = 128;
-constexpr int kNT = 256;
+constexpr int kNT = 384;   // warps 0-7: intra-chunk group, warps 8-11: recurrence group
+constexpr int kNI = 256;   // intra-group threads
 
 constexpr uint32_t TMEM_COLS = 512;
 constexpr int LT = 68;   // row stride (floats) of the fp32 64x64 scratch: 16-byte aligned rows
@@ -63,7 +64,20 @@ __device__ __forceinline__ void unpack8(const uint4& u, float* x) {
   }
 }
 
-// Store 32 fp32 values (scaled by f[j]) as 4 bf16 chunks of row r, chunks cc0..cc0+3.
+// Store 16 fp32 values as 2 bf16 chunks of row r, chunks cc0, cc0+1.
+__device__ __forceinline__ void store_row16(uint8_t* tile, int R, int r, int cc0, const float* v) {
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    uint4 u;
+    u.x = pack2(v[8 * q + 0], v[8 * q + 1]);
+    u.y = pack2(v[8 * q + 2], v[8 * q + 3]);
+    u.z = pack2(v[8 * q + 4], v[8 * q + 5]);
+    u.w = pack2(v[8 * q + 6], v[8 * q + 7]);
+    *reinterpret_cast<uint4*>(tile + chunk_off(r, cc0 + q, R)) = u;
+  }
+}
+
+// Store 32 fp32 values as 4 bf16 chunks of row r, chunks cc0..cc0+3.
 __device__ __forceinline__ void store_row32(uint8_t* tile, int R, int r, int cc0, const float* v) {
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
@@ -91,31 +105,35 @@ __device__ __forceinline__ float lds1(const float* p) {
 __device__ __forceinline__ float f4get(const float4& v, int i) {
   return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
 }
-// Barrier over one 128-thread warpgroup (ids 1 and 2; id 0 is __syncthreads).
-__device__ __forceinline__ void group_sync(int id) { asm volatile("bar.sync %0, 128;" ::"r"(id) : "memory"); }
+// Named barrier over one warp group (id 1: the 256 intra threads, id 2: the 128 recurrence threads).
+__device__ __forceinline__ void group_sync(int id) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(id == 1 ? kNI : 128) : "memory");
+}
 
 // T = (I - X)^-1 for the strictly lower 64x64 X held in fp32 shared memory (row stride LT), in
 // place, by the blocked scheme of src/gdn_chunk_fast.py:33-62: 16x16 diagonal blocks by the row
-// recurrence (evaluated column-wise), then pairwise merges T21 = (B X21) A.  Run by one warpgroup
-// (4 warps, `gid` its named barrier); P is 32 x LP floats of scratch.  In the merges a lane owns
+// recurrence (evaluated column-wise), then pairwise merges T21 = (B X21) A.  Run by the 8 warps of
+// the intra group (named barrier 1); P is 32 x LP floats of scratch.  In the merges a lane owns
 // one output column: the column operand is one conflict-free 32-bit load per row and the row
 // operand a uniform-address float4, which keeps the shared-memory wavefront count low.
-__device__ __forceinline__ void tri_inverse64(float* X, float* P, int warp, int lane, int gid) {
-  {  // diagonal block `warp`; lane j < 16 owns column j
+__device__ __forceinline__ void tri_inverse64(float* X, float* P, int warp, int lane) {
+  if (warp < 4) {  // diagonal block `warp`; lane j < 16 owns column j
     const int b0 = 16 * warp, j = lane & 15;
     float acc[16], r[16];
-    float4 xr[16][4];
 #pragma unroll
     for (int i = 0; i < 16; ++i) acc[i] = lds1(X + (b0 + i) * LT + b0 + j);
 #pragma unroll
-    for (int i = 0; i < 16; ++i)
+    for (int mg = 0; mg < 4; ++mg) {
+      float4 xr[16];
 #pragma unroll
-      for (int q = 0; q < 4; ++q) xr[i][q] = lds4(X + (b0 + i) * LT + b0 + 4 * q);
+      for (int i = 0; i < 16; ++i) xr[i] = lds4(X + (b0 + i) * LT + b0 + 4 * mg);
 #pragma unroll
-    for (int m = 0; m < 16; ++m) {
-      r[m] = m > j ? acc[m] : 0.f;
+      for (int mm = 0; mm < 4; ++mm) {
+        const int m = 4 * mg + mm;
+        r[m] = m > j ? acc[m] : 0.f;
 #pragma unroll
-      for (int i = m + 1; i < 16; ++i) acc[i] = fmaf(f4get(xr[i][m >> 2], m & 3), r[m], acc[i]);
+        for (int i = m + 1; i < 16; ++i) acc[i] = fmaf(f4get(xr[i], mm), r[m], acc[i]);
+      }
     }
     __syncwarp();
     if (lane < 16) {
@@ -123,76 +141,74 @@ __device__ __forceinline__ void tri_inverse64(float* X, float* P, int warp, int 
       for (int i = 0; i < 16; ++i) X[(b0 + i) * LT + b0 + j] = i == j ? 1.f : (i > j ? r[i] : 0.f);
     }
   }
-  group_sync(gid);
-  {  // level 1: merge m = lane / 16 (blocks (0,1) or (2,3)), column c = lane % 16, rows 4w..4w+3
-    const int m = lane >> 4, c = lane & 15, lo = m * 32, hi = lo + 16, r0 = 4 * warp;
-    float a[4] = {0.f, 0.f, 0.f, 0.f};
+  group_sync(1);
+  {  // level 1: merge m = lane / 16 (blocks (0,1) or (2,3)), column c = lane % 16, rows 2w, 2w+1
+    const int m = lane >> 4, c = lane & 15, lo = m * 32, hi = lo + 16, r0 = 2 * warp;
+    float a[2] = {0.f, 0.f};
 #pragma unroll
     for (int tq = 0; tq < 4; ++tq) {
       float x[4];
 #pragma unroll
       for (int u = 0; u < 4; ++u) x[u] = lds1(X + (hi + 4 * tq + u) * LT + lo + c);
 #pragma unroll
-      for (int rr = 0; rr < 4; ++rr) {
+      for (int rr = 0; rr < 2; ++rr) {
         const float4 bv = lds4(X + (hi + r0 + rr) * LT + hi + 4 * tq);
         a[rr] = fmaf(bv.w, x[3], fmaf(bv.z, x[2], fmaf(bv.y, x[1], fmaf(bv.x, x[0], a[rr]))));
       }
     }
 #pragma unroll
-    for (int rr = 0; rr < 4; ++rr) P[m * 16 * LP + (r0 + rr) * LP + c] = a[rr];
-    group_sync(gid);
-#pragma unroll
-    for (int rr = 0; rr < 4; ++rr) a[rr] = 0.f;
+    for (int rr = 0; rr < 2; ++rr) P[m * 16 * LP + (r0 + rr) * LP + c] = a[rr];
+    group_sync(1);
+    a[0] = 0.f;
+    a[1] = 0.f;
 #pragma unroll
     for (int tq = 0; tq < 4; ++tq) {
       float x[4];
 #pragma unroll
       for (int u = 0; u < 4; ++u) x[u] = lds1(X + (lo + 4 * tq + u) * LT + lo + c);
 #pragma unroll
-      for (int rr = 0; rr < 4; ++rr) {
+      for (int rr = 0; rr < 2; ++rr) {
         const float4 pv = lds4(P + m * 16 * LP + (r0 + rr) * LP + 4 * tq);
         a[rr] = fmaf(pv.w, x[3], fmaf(pv.z, x[2], fmaf(pv.y, x[1], fmaf(pv.x, x[0], a[rr]))));
       }
     }
 #pragma unroll
-    for (int rr = 0; rr < 4; ++rr) X[(hi + r0 + rr) * LT + lo + c] = a[rr];
-    group_sync(gid);
+    for (int rr = 0; rr < 2; ++rr) X[(hi + r0 + rr) * LT + lo + c] = a[rr];
+    group_sync(1);
   }
-  {  // level 2: column c = lane, rows 8w .. 8w+7
-    const int c = lane, r0 = 8 * warp;
-    float a[8];
-#pragma unroll
-    for (int rr = 0; rr < 8; ++rr) a[rr] = 0.f;
+  {  // level 2: column c = lane, rows 4w .. 4w+3
+    const int c = lane, r0 = 4 * warp;
+    float a[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int tq = 0; tq < 8; ++tq) {
       float x[4];
 #pragma unroll
       for (int u = 0; u < 4; ++u) x[u] = lds1(X + (32 + 4 * tq + u) * LT + c);
 #pragma unroll
-      for (int rr = 0; rr < 8; ++rr) {
+      for (int rr = 0; rr < 4; ++rr) {
         const float4 bv = lds4(X + (32 + r0 + rr) * LT + 32 + 4 * tq);
         a[rr] = fmaf(bv.w, x[3], fmaf(bv.z, x[2], fmaf(bv.y, x[1], fmaf(bv.x, x[0], a[rr]))));
       }
     }
 #pragma unroll
-    for (int rr = 0; rr < 8; ++rr) P[(r0 + rr) * LP + c] = a[rr];
-    group_sync(gid);
+    for (int rr = 0; rr < 4; ++rr) P[(r0 + rr) * LP + c] = a[rr];
+    group_sync(1);
 #pragma unroll
-    for (int rr = 0; rr < 8; ++rr) a[rr] = 0.f;
+    for (int rr = 0; rr < 4; ++rr) a[rr] = 0.f;
 #pragma unroll
     for (int tq = 0; tq < 8; ++tq) {
       float x[4];
 #pragma unroll
       for (int u = 0; u < 4; ++u) x[u] = lds1(X + (4 * tq + u) * LT + c);
 #pragma unroll
-      for (int rr = 0; rr < 8; ++rr) {
+      for (int rr = 0; rr < 4; ++rr) {
         const float4 pv = lds4(P + (r0 + rr) * LP + 4 * tq);
         a[rr] = fmaf(pv.w, x[3], fmaf(pv.z, x[2], fmaf(pv.y, x[1], fmaf(pv.x, x[0], a[rr]))));
       }
     }
 #pragma unroll
-    for (int rr = 0; rr < 8; ++rr) X[(32 + r0 + rr) * LT + c] = a[rr];
-    group_sync(gid);
+    for (int rr = 0; rr < 4; ++rr) X[(32 + r0 + rr) * LT + c] = a[rr];
+    group_sync(1);
   }
 }
 
@@ -252,8 +268,9 @@ __global__ void __launch_bounds__(kNT, 1)
 
   const int h = blockIdx.x, b = blockIdx.y;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int grp = warp >> 2;          // 0: intra-chunk group, 1: recurrence group
-  const int wg = warp & 3;            // warp within the group = TMEM lane quarter
+  const int grp = warp >= 8 ? 1 : 0;  // 0: intra-chunk group (warps 0-7), 1: recurrence group (8-11)
+  const int wg = warp & 3;            // TMEM lane quarter this warp may access
+  const int hv = (warp >> 2) & 1;     // intra group: which half of the columns this warp handles
   const int row = 32 * wg + lane;     // TMEM lane of this thread
   const uint32_t lane_off = uint32_t(32 * wg) << 16;
   const int hk = h / (p.Hv / p.Hk);
@@ -360,7 +377,7 @@ __global__ void __launch_bounds__(kNT, 1)
       }
       if (ok && !mbar_wait(bar_qk0 + 8 * bf, uint32_t(ci >> 1) & 1u)) ok = false;
       if (nt < kC) {  // zero the q/k rows past the sequence end (they hold the next sequence)
-        for (int i = tid; i < (kC - nt) * 32; i += 128) {
+        for (int i = tid; i < (kC - nt) * 32; i += kNI) {
           const int r = nt + (i >> 5), tile = (i >> 3) & 3, cc = i & 7;
           *reinterpret_cast<uint4*>(qk + tile * 8192 + chunk_off(r, cc, 128)) = make_uint4(0, 0, 0, 0);
         }
@@ -379,7 +396,7 @@ __global__ void __launch_bounds__(kNT, 1)
       if (ok && !mbar_wait(bar_mi, ph_mi)) ok = false;
       ph_mi ^= 1u;
       tc_fence_after();
-      {  // l2-norm factors from the diagonal (bf16 arithmetic as the reference's l2norm)
+      if (hv == 0) {  // l2-norm factors from the diagonal (bf16 arithmetic as the reference's l2norm)
         float dg[32];
         tmem_ld32(tmem + T_P1 + lane_off + 32 * wg, dg);
         float ss = dg[0];
@@ -396,8 +413,8 @@ __global__ void __launch_bounds__(kNT, 1)
         cv.bwc[tid] = cv.bt[tid] * cv.egc[tid] * rk;
       }
       {  // P1 epilogue: QKm tile (rows 0-63) and X (rows 64-127), from the K columns 64-127
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {
+        {
+          const int half = hv;
           float a[32];
           tmem_ld32(tmem + T_P1 + lane_off + 64 + 32 * half, a);
           if (row < 64) {
@@ -421,12 +438,12 @@ __global__ void __launch_bounds__(kNT, 1)
         }
       }
       group_sync(1);
-      tri_inverse64(Xs, Ps, wg, lane, 1);
-      {  // B_U = T diag(beta), B_W = T diag(beta e^gc rk): thread -> row t, 32 columns
-        const int t = tid >> 1, cb = (tid & 1) * 32;
-        float u[32], w[32];
+      tri_inverse64(Xs, Ps, warp, lane);
+      {  // B_U = T diag(beta), B_W = T diag(beta e^gc rk): thread -> row t, 16 columns
+        const int t = tid >> 2, cb = (tid & 3) * 16;
+        float u[16], w[16];
 #pragma unroll
-        for (int e4 = 0; e4 < 8; ++e4) {
+        for (int e4 = 0; e4 < 4; ++e4) {
           const float4 tv4 = lds4(Xs + t * LT + cb + 4 * e4);
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
@@ -436,12 +453,12 @@ __global__ void __launch_bounds__(kNT, 1)
             w[4 * e4 + e] = tv * cv.bwc[s];
           }
         }
-        store_row32(sm + W_BU, 64, t, cb >> 3, u);
-        store_row32(sm + W_BW, 64, t, cb >> 3, w);
+        store_row16(sm + W_BU, 64, t, cb >> 3, u);
+        store_row16(sm + W_BW, 64, t, cb >> 3, w);
       }
       if (ok && !mbar_wait(bar_v, uint32_t(ci) & 1u)) ok = false;
       if (nt < kC) {
-        for (int i = tid; i < (kC - nt) * 16; i += 128) {
+        for (int i = tid; i < (kC - nt) * 16; i += kNI) {
           const int r = nt + (i >> 4), tile = (i >> 3) & 1, cc = i & 7;
           *reinterpret_cast<uint4*>(sm + W_V + tile * 8192 + chunk_off(r, cc, 64)) = make_uint4(0, 0, 0, 0);
         }
@@ -475,7 +492,7 @@ __global__ void __launch_bounds__(kNT, 1)
     }
   } else {
     // ======================================================================== recurrence group
-    const int rt = tid - 128;
+    const int rt = tid - kNI;
     uint32_t ph_mr = 0;
     {  // initial state -> TMEM (thread: row k, all 128 columns)
       float v[32];
