@@ -1,0 +1,313 @@
+"""Slot-based continuous-batching engine for the hybrid Qwen3.5 model on B200.
+
+Same public interface as the reference's ``CBEngine`` (src/cb_engine.py:80-355):
+``CBEngine(model, n_slots, t_max, device, graph_decode=False, tp=1)`` with ``prefill(slot, ids)``,
+``prefill_batch(slots, id_list)``, ``decode_step(slots, tokens)`` and ``free(slot)``, plus the
+``prefill_chunk(slot, ids, start, last)`` of the reference's ``TPEngine`` (src/cb_tp.py:195-271).
+
+What changes on B200:
+  * GDN layers call the slot-indexed CUDA kernels: prefill writes the final recurrent state and
+    the conv window straight into the slot's pool rows (no cache copy, src/cb_engine.py:198-205);
+    decode runs one fused kernel pair per layer that gathers and scatters the state in-kernel.
+  * ``prefill_batch`` packs prompts back to back (``cu_seqlens``) instead of left padding them
+    (src/cb_engine.py:210-242).
+  * Decode always covers all N slots, as the reference does (src/cb_engine.py:245-252), but an
+    inactive slot's GDN update goes to a scratch pool row (index N) through the slot index, so
+    slots that are idle or in the middle of a chunked prefill are left exactly as they were; the
+    reference needs ``hold`` save/restore for that (src/cb_tp.py:273-285).
+  * Decode steps are captured in CUDA graphs, one per attention-length bucket, from one shared
+    memory pool (src/cb_engine.py:123-187).
+Attention, MLP, norms, embeddings and the LM head are HF's own modules, as in the reference.
+"""
+from __future__ import annotations
+
+import os
+
+import torch
+import torch.nn.functional as F
+
+from . import ops
+
+# Decode conv rounding: False = HF torch_causal_conv1d_update (one rounding of the fp32 sum);
+# True = the reference's elem_conv_update (products and sum rounded in bf16).  Set by the caller
+# exactly like the reference's cb_engine.ELEM_CONV (src/cb_engine.py:25).
+ELEM_CONV = False
+
+# One captured decode graph per attention-length bucket of this many tokens (src/cb_engine.py:28).
+GRAPH_BUCKET = int(os.environ.get("CB_GRAPH_BUCKET", "512"))
+
+
+class CBEngine:
+    def __init__(self, model, n_slots, t_max, device, graph_decode=False, tp=1):
+        from transformers.models.qwen3_5 import modeling_qwen3_5 as M
+        self.M = M
+        self.model = model
+        self.lm = model.model.language_model
+        cfg = model.config.text_config
+        self.cfg = cfg
+        self.dev = torch.device(device)
+        if self.dev.type != "cuda":
+            raise RuntimeError("the B200 engine runs on CUDA devices only")
+        self.N = n_slots
+        self.T = t_max
+        self.tp = tp
+        self.K = cfg.linear_conv_kernel_dim
+        self.lens = [0] * n_slots
+        bf = torch.bfloat16
+        self.kv_k, self.kv_v, self.conv, self.rec, self.gdn = {}, {}, {}, {}, {}
+        ws_bytes = 0
+        for i, t in enumerate(cfg.layer_types):
+            layer = self.lm.layers[i]
+            if t == "full_attention":
+                at = layer.self_attn
+                kvh = at.k_proj.weight.shape[0] // at.head_dim
+                # row N is a scratch row: never read as a real slot
+                self.kv_k[i] = torch.zeros(n_slots + 1, kvh, t_max, at.head_dim, dtype=bf, device=self.dev)
+                self.kv_v[i] = torch.zeros(n_slots + 1, kvh, t_max, at.head_dim, dtype=bf, device=self.dev)
+            else:
+                gd = layer.linear_attn
+                Hk, Hv, dk, dv = gd.num_k_heads, gd.num_v_heads, gd.head_k_dim, gd.head_v_dim
+                self.conv[i] = torch.zeros(n_slots + 1, gd.conv_dim, self.K, dtype=bf, device=self.dev)
+                self.rec[i] = torch.zeros(n_slots + 1, Hv, dk, dv, dtype=torch.float32, device=self.dev)
+                self.gdn[i] = dict(
+                    Hk=Hk, Hv=Hv, dk=dk, dv=dv,
+                    A_log=gd.A_log.detach().float().contiguous(),
+                    dt_bias=gd.dt_bias.detach().float().contiguous(),
+                    conv_w=gd.conv1d.weight.detach().squeeze(1).contiguous(),
+                    conv_b=None if gd.conv1d.bias is None else gd.conv1d.bias.detach().contiguous(),
+                    norm_w=gd.norm.weight.detach().to(bf).contiguous(),
+                    eps=float(getattr(gd.norm, "variance_epsilon", getattr(gd.norm, "eps", 1e-6))))
+                ws_bytes = max(ws_bytes, ops.decode_layer_workspace_bytes(n_slots, Hk, Hv, dk, dv, bf))
+        self._ws = torch.empty(max(ws_bytes, 256), dtype=torch.uint8, device=self.dev)
+        self._tok = torch.zeros(n_slots, dtype=torch.long, device=self.dev)
+        self._pos = torch.zeros(n_slots, dtype=torch.long, device=self.dev)
+        self._slot = torch.arange(n_slots, dtype=torch.int32, device=self.dev)
+        self._all_idx = torch.arange(n_slots, dtype=torch.long, device=self.dev)
+        self._head_off = {}
+        self.graph_decode = graph_decode
+        self._graphs, self._graph_out = {}, {}
+        if graph_decode:
+            self._capture_graphs()
+
+    # ------------------------------------------------------------------ graph decode
+    def _buckets(self):
+        b = list(range(GRAPH_BUCKET, self.T + 1, GRAPH_BUCKET))
+        if not b or b[-1] < self.T:
+            b.append(self.T)
+        return b
+
+    def _bucket(self, L):
+        for b in self._buckets():
+            if b >= L:
+                return b
+        raise ValueError(f"decode length {L} > T {self.T}")
+
+    def _capture_graphs(self):
+        """One CUDA graph per attention-length bucket, all from one memory pool; must run before
+        any prefill (state written by warm-up and capture is zeroed afterwards)."""
+        pool = torch.cuda.graph_pool_handle()
+        with torch.inference_mode():
+            self._core(self._buckets()[0])               # eager warm-up outside capture
+            torch.cuda.synchronize(self.dev)
+            for b in self._buckets():
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, pool=pool):
+                    out = self._core(b)
+                self._graphs[b], self._graph_out[b] = g, out
+            torch.cuda.synchronize(self.dev)
+            self._reset_state()
+
+    def _reset_state(self):
+        for d in (self.kv_k, self.kv_v, self.conv, self.rec):
+            for t in d.values():
+                t.zero_()
+        self.lens = [0] * self.N
+
+    # ------------------------------------------------------------------ decode
+    def _kv_rows(self, pos):
+        # flat row index into kv.view(-1, hd) for (slot i, kv head, position pos[i]), i = 0..N-1
+        kvh = next(iter(self.kv_k.values())).shape[1]
+        if "off" not in self._head_off:
+            self._head_off["off"] = (torch.arange(kvh, device=self.dev) * self.T)[None, :]
+        return (self._all_idx[:, None] * (kvh * self.T) + self._head_off["off"] + pos[:, None]).reshape(-1)
+
+    def _attn(self, at, i, h, cos, sin, pos, Lmax, mask):
+        n = h.shape[0]
+        hd = at.head_dim
+        kvh = self.kv_k[i].shape[1]
+        qg = at.q_proj(h).view(n, 1, -1, hd * 2)
+        q, gate = torch.chunk(qg, 2, dim=-1)
+        gate = gate.reshape(n, 1, -1)
+        q = at.q_norm(q).transpose(1, 2)
+        k = at.k_norm(at.k_proj(h).view(n, 1, kvh, hd)).transpose(1, 2)
+        v = at.v_proj(h).view(n, 1, kvh, hd).transpose(1, 2)
+        q, k = self.M.apply_rotary_pos_emb(q, k, cos, sin)
+        rows = self._kv_rows(pos)
+        self.kv_k[i].view(-1, hd).index_copy_(0, rows, k[:, :, 0, :].reshape(-1, hd))
+        self.kv_v[i].view(-1, hd).index_copy_(0, rows, v[:, :, 0, :].reshape(-1, hd))
+        Kg = self.kv_k[i][:n, :, :Lmax]
+        Vg = self.kv_v[i][:n, :, :Lmax]
+        g = q.shape[1] // kvh
+        qk = q.reshape(n, kvh, g, hd)
+        o = F.scaled_dot_product_attention(qk, Kg, Vg, attn_mask=mask.expand(n, 1, g, Lmax), scale=at.scaling)
+        o = o.reshape(n, 1, -1) * torch.sigmoid(gate)
+        return at.o_proj(o)
+
+    def _gdn(self, gd, i, h):
+        n = h.shape[0]
+        p = self.gdn[i]
+        mixed = gd.in_proj_qkv(h).reshape(n, -1)
+        z = gd.in_proj_z(h).reshape(n, p["Hv"], p["dv"])
+        b = gd.in_proj_b(h).reshape(n, -1)
+        a = gd.in_proj_a(h).reshape(n, -1)
+        core = ops.decode_layer(mixed, z, a, b, p["A_log"], p["dt_bias"], p["conv_w"], p["conv_b"], self.conv[i],
+                                self.rec[i], self._slot, p["norm_w"], p["eps"], p["Hk"], p["Hv"], p["dk"], p["dv"],
+                                ops.GDN_CONV_ELEM if ELEM_CONV else ops.GDN_CONV_HF, workspace=self._ws)
+        return gd.out_proj(core.reshape(n, 1, -1))
+
+    def _core(self, Lmax):
+        """One decode step for all N slots from the static buffers (capturable)."""
+        N, pos = self.N, self._pos
+        mask = (torch.arange(Lmax, device=self.dev)[None, :] <= pos[:, None])[:, None, None, :]
+        x = self.lm.embed_tokens(self._tok[:, None])
+        pos3 = pos.view(1, N, 1).expand(3, N, 1)
+        cos, sin = self.lm.rotary_emb(x, pos3)
+        for i, layer in enumerate(self.lm.layers):
+            h = layer.input_layernorm(x)
+            if self.cfg.layer_types[i] == "full_attention":
+                h = self._attn(layer.self_attn, i, h, cos, sin, pos, Lmax, mask)
+            else:
+                h = self._gdn(layer.linear_attn, i, h)
+            x = x + h
+            x = x + layer.mlp(layer.post_attention_layernorm(x))
+        x = self.lm.norm(x)
+        return self.model.lm_head(x[:, 0]).argmax(-1)
+
+    @torch.inference_mode()
+    def decode_step(self, slots, tokens, hold=()):
+        """One token for each slot in ``slots``; returns the next token per slot.  All N slots are
+        computed (dense, as the reference); slots not in ``slots`` write their GDN update to the
+        scratch row, so their conv/recurrent state is untouched (``hold`` is accepted for
+        interface parity with TPEngine.decode_step and needs no save/restore)."""
+        N = self.N
+        tok_full = [0] * N
+        slot_map = [N] * N
+        for s, t in zip(slots, tokens):
+            tok_full[s] = int(t)
+            slot_map[s] = s
+        L = max(self.lens[s] for s in slots) + 1 if slots else 1
+        if L > self.T:
+            raise ValueError(f"decode length {L} > T {self.T}")
+        self._pos.copy_(torch.tensor(self.lens, dtype=torch.long))
+        self._tok.copy_(torch.tensor(tok_full, dtype=torch.long))
+        self._slot.copy_(torch.tensor(slot_map, dtype=torch.int32))
+        if self.graph_decode:
+            b = self._bucket(L)
+            self._graphs[b].replay()
+            nxt = self._graph_out[b].tolist()
+        else:
+            nxt = self._core(L).tolist()
+        for s in slots:
+            self.lens[s] += 1
+        return [nxt[s] for s in slots]
+
+    # ------------------------------------------------------------------ prefill
+    def _attn_prefill(self, at, i, h, cos, sin, slots, starts, cu):
+        T = h.shape[1]
+        hd = at.head_dim
+        kvh = self.kv_k[i].shape[1]
+        qg = at.q_proj(h).view(1, T, -1, hd * 2)
+        q, gate = torch.chunk(qg, 2, dim=-1)
+        gate = gate.reshape(1, T, -1)
+        q = at.q_norm(q).transpose(1, 2)
+        k = at.k_norm(at.k_proj(h).view(1, T, kvh, hd)).transpose(1, 2)
+        v = at.v_proj(h).view(1, T, kvh, hd).transpose(1, 2)
+        q, k = self.M.apply_rotary_pos_emb(q, k, cos, sin)
+        g = q.shape[1] // kvh
+        o = torch.empty_like(q)
+        for b, slot in enumerate(slots):
+            s, e, st = cu[b], cu[b + 1], starts[b]
+            L = e - s
+            self.kv_k[i][slot, :, st:st + L] = k[0, :, s:e]
+            self.kv_v[i][slot, :, st:st + L] = v[0, :, s:e]
+            kr = self.kv_k[i][slot:slot + 1, :, :st + L].repeat_interleave(g, dim=1)
+            vr = self.kv_v[i][slot:slot + 1, :, :st + L].repeat_interleave(g, dim=1)
+            if st == 0:
+                o[:, :, s:e] = F.scaled_dot_product_attention(q[:, :, s:e], kr, vr, is_causal=True, scale=at.scaling)
+            else:
+                qpos = torch.arange(st, st + L, device=self.dev)
+                kpos = torch.arange(st + L, device=self.dev)
+                causal = (kpos[None, :] <= qpos[:, None])[None, None]
+                o[:, :, s:e] = F.scaled_dot_product_attention(q[:, :, s:e], kr, vr, attn_mask=causal,
+                                                              scale=at.scaling)
+        o = o.transpose(1, 2).reshape(1, T, -1) * torch.sigmoid(gate)
+        return at.o_proj(o)
+
+    def _gdn_prefill(self, gd, i, h, cu_d, slot_t, use_init):
+        T = h.shape[1]
+        p = self.gdn[i]
+        Hk, Hv, dk, dv = p["Hk"], p["Hv"], p["dk"], p["dv"]
+        mixed = gd.in_proj_qkv(h)[0]
+        z = gd.in_proj_z(h)[0].reshape(T, Hv, dv)
+        b = gd.in_proj_b(h)[0]
+        a = gd.in_proj_a(h)[0]
+        y = ops.prefill_conv_varlen(mixed, cu_d, p["conv_w"], p["conv_b"], self.conv[i], slot_t, use_init)
+        q = y[:, :Hk * dk].view(T, Hk, dk)
+        k = y[:, Hk * dk:2 * Hk * dk].view(T, Hk, dk)
+        v = y[:, 2 * Hk * dk:].view(T, Hv, dv)
+        beta = b.sigmoid().float()
+        g = -p["A_log"].exp() * F.softplus(a.float() + p["dt_bias"])
+        core = ops.chunk_prefill_varlen(q, k, v, g, beta, cu_d, self.rec[i], slot_t, use_init, True)
+        core = ops.gated_rmsnorm(core, z, p["norm_w"], p["eps"])
+        return gd.out_proj(core.reshape(1, T, -1))
+
+    @torch.inference_mode()
+    def prefill_batch(self, slots, id_list, starts=None):
+        """Prefill several prompts in one packed forward (no padding).  ``starts`` (optional)
+        continues sequences whose first ``starts[b]`` tokens are already in their slot (chunked
+        prefill).  Returns the greedy next token per prompt."""
+        B = len(slots)
+        starts = [0] * B if starts is None else [int(s) for s in starts]
+        ids = [x.reshape(-1).to(self.dev) for x in id_list]
+        lens = [int(x.numel()) for x in ids]
+        for st, L in zip(starts, lens):
+            if st + L >= self.T:
+                raise ValueError(f"prompt {st + L} >= T {self.T}")
+        cu = [0]
+        for L in lens:
+            cu.append(cu[-1] + L)
+        cu_d = torch.tensor(cu, dtype=torch.int32, device=self.dev)
+        slot_t = torch.tensor(slots, dtype=torch.int32, device=self.dev)
+        use_init = torch.tensor([1 if st > 0 else 0 for st in starts], dtype=torch.int32, device=self.dev)
+        pos = torch.cat([torch.arange(st, st + L, device=self.dev) for st, L in zip(starts, lens)])
+        x = self.lm.embed_tokens(torch.cat(ids)[None])
+        T = x.shape[1]
+        cos, sin = self.lm.rotary_emb(x, pos.view(1, 1, T).expand(3, 1, T))
+        for i, layer in enumerate(self.lm.layers):
+            h = layer.input_layernorm(x)
+            if self.cfg.layer_types[i] == "full_attention":
+                h = self._attn_prefill(layer.self_attn, i, h, cos, sin, slots, starts, cu)
+            else:
+                h = self._gdn_prefill(layer.linear_attn, i, h, cu_d, slot_t, use_init)
+            x = x + h
+            x = x + layer.mlp(layer.post_attention_layernorm(x))
+        last = torch.tensor([c - 1 for c in cu[1:]], dtype=torch.long, device=self.dev)
+        xl = self.lm.norm(x[0, last])
+        firsts = self.model.lm_head(xl).argmax(-1).tolist()
+        for slot, st, L in zip(slots, starts, lens):
+            self.lens[slot] = st + L
+        return firsts
+
+    def prefill(self, slot, ids):
+        """ids: [1, L] (or [L]). Returns the first generated token (greedy)."""
+        return self.prefill_batch([slot], [ids])[0]
+
+    def prefill_chunk(self, slot, ids, start, last):
+        """Prefill tokens [start, start + C) of one prompt into ``slot``; earlier chunks must already
+        be in the slot.  Returns the first generated token when ``last``, else None
+        (src/cb_tp.py:195-271)."""
+        first = self.prefill_batch([slot], [ids], starts=[start])[0]
+        return first if last else None
+
+    def free(self, slot):
+        self.lens[slot] = 0

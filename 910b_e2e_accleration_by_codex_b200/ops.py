@@ -106,16 +106,19 @@ def _conv_update(x, state, weight, bias, mode, slot_idx=None, out=None, err=None
     wd = weight.dtype
     if x.dtype != wd:
         x = x.to(wd)
-    if state.dtype != wd or not state.is_contiguous():
-        raise ValueError("conv state must be a contiguous tensor of the weight's dtype (updated in place)")
+    # the kernel updates a contiguous [slots, C, K] pool in place; other layouts (HF's cache may
+    # hold a strided view) go through a contiguous copy that is written back
+    st = state if (state.dtype == wd and state.is_contiguous()) else state.to(wd).contiguous()
     w = weight.contiguous()
     b = None if bias is None else bias.to(wd).contiguous()
     y = torch.empty(B, Cc, T, dtype=wd, device=x.device) if out is None else out
-    n_slots = state.shape[0]
+    n_slots = st.shape[0]
     lib = _lib.load()
-    _lib.check(lib.gdn_conv_update(_p(x), x.stride(0), x.stride(1), x.stride(2), _p(state), _p(_i32(slot_idx)),
+    _lib.check(lib.gdn_conv_update(_p(x), x.stride(0), x.stride(1), x.stride(2), _p(st), _p(_i32(slot_idx)),
                                    n_slots, _p(w), _p(b), _p(y), y.stride(0), y.stride(1), y.stride(2), B, Cc, T,
                                    K, 1, mode, _dtype_code(w), _p(err), _stream()), "gdn_conv_update")
+    if st is not state:
+        state.copy_(st)
     return y
 
 
@@ -276,10 +279,14 @@ def prefill_conv_varlen(x, cu_seqlens, weight, bias=None, conv_pool=None, slot_i
 
 
 # ============================================================================ fused decode layer
+def decode_layer_workspace_bytes(n, Hk, Hv, dk, dv, dtype) -> int:
+    """Bytes of device workspace ``decode_layer`` needs (the conv output between its kernels)."""
+    return int(_lib.load().gdn_decode_layer_workspace_size(n, Hk, Hv, dk, dv, _DT[dtype]))
+
+
 def decode_layer_workspace(n, Hk, Hv, dk, dv, dtype, device):
-    """Device workspace for ``decode_layer`` (the conv output between its two kernels)."""
-    nbytes = _lib.load().gdn_decode_layer_workspace_size(n, Hk, Hv, dk, dv, _DT[dtype])
-    return torch.empty(nbytes, dtype=torch.uint8, device=device)
+    """Device workspace for ``decode_layer``."""
+    return torch.empty(decode_layer_workspace_bytes(n, Hk, Hv, dk, dv, dtype), dtype=torch.uint8, device=device)
 
 
 def decode_layer(mixed_qkv, z, a, b, A_log, dt_bias, conv_w, conv_b, conv_pool, rec_pool, slot_idx, norm_w,

@@ -225,12 +225,80 @@ def make_gates(ref, seed):
     save("gates_bf16.npz", dict(a=a, b=b, A_log=A_log, dt_bias=dt_bias, beta=beta, g=g))
 
 
+ENGINE_TEXT_CONFIG = dict(
+    vocab_size=256, hidden_size=128, intermediate_size=256, num_hidden_layers=4, num_attention_heads=2,
+    num_key_value_heads=1, head_dim=64, linear_num_key_heads=1, linear_num_value_heads=2,
+    linear_key_head_dim=128, linear_value_head_dim=128, linear_conv_kernel_dim=4,
+    layer_types=["linear_attention", "linear_attention", "linear_attention", "full_attention"],
+    max_position_embeddings=512, rms_norm_eps=1e-6, attention_bias=False, hidden_act="silu")
+ENGINE_VISION_CONFIG = dict(depth=1, hidden_size=32, num_heads=2, intermediate_size=64, out_hidden_size=128)
+
+
+def tiny_model(seed=0):
+    """A tiny random Qwen3.5 (3 GDN : 1 attention, GDN heads of 128) in bf16; weights from HF's
+    own init under `seed` with the gate projections scaled up so logits are not near-ties."""
+    from transformers.models.qwen3_5.configuration_qwen3_5 import Qwen3_5Config
+    from transformers.models.qwen3_5.modeling_qwen3_5 import Qwen3_5ForConditionalGeneration
+    torch.manual_seed(seed)
+    cfg = Qwen3_5Config(text_config=ENGINE_TEXT_CONFIG, vision_config=ENGINE_VISION_CONFIG)
+    model = Qwen3_5ForConditionalGeneration(cfg)
+    with torch.no_grad():
+        for name, p in model.named_parameters():
+            if p.dim() == 2 and "visual" not in name:
+                p.mul_(4.0)
+    return model.to(torch.bfloat16).eval()
+
+
+def make_engine(ref, seed):
+    """Reference CBEngine (src/cb_engine.py:80-355) on a tiny model, on the CPU, with the
+    reference's GDN plug-ins (v2 chunk prefill, recurrent_single_step) and HF's gated norm: two
+    prompts prefilled into slots 1 and 0, then 5 dense decode steps with both slots active.
+    Stores the weights, the tokens, the logits of every step and the GDN slot states."""
+    import cb_engine
+    M = ref["M"]
+    model = tiny_model(seed)
+    for m in model.modules():
+        if isinstance(m, M.Qwen3_5GatedDeltaNet):
+            m.recurrent_gated_delta_rule = ref["rec1"]
+            m.chunk_gated_delta_rule = ref["v2"]
+    cb_engine.ELEM_CONV = False
+    logits = []
+    hook = model.lm_head.register_forward_hook(lambda mod, inp, out: logits.append(out.detach().float().clone()))
+    eng = cb_engine.CBEngine(model, n_slots=2, t_max=128, device="cpu")
+    gen = torch.Generator().manual_seed(seed + 1)
+    ids_a = torch.randint(0, 256, (1, 37), generator=gen)
+    ids_b = torch.randint(0, 256, (1, 23), generator=gen)
+    first_a = eng.prefill(1, ids_a)
+    first_b = eng.prefill(0, ids_b)
+    pre_logits = [logits[0][0, -1], logits[1][0, -1]]
+    gdn_layers = sorted(eng.rec)
+    rec_pre = torch.stack([eng.rec[i][:2].clone() for i in gdn_layers])
+    conv_pre = torch.stack([eng.conv[i][:2].clone() for i in gdn_layers])
+    logits.clear()
+    toks = [[first_b, first_a]]
+    for _ in range(5):
+        toks.append(eng.decode_step([0, 1], toks[-1]))
+    hook.remove()
+    dec_logits = torch.stack([lg for lg in logits])            # [5, 2, vocab]
+    rec_post = torch.stack([eng.rec[i][:2].clone() for i in gdn_layers])
+    conv_post = torch.stack([eng.conv[i][:2].clone() for i in gdn_layers])
+    sd = {f"w::{k}": v for k, v in model.state_dict().items()}
+    save("engine_tiny.npz", dict(ids_a=ids_a[0], ids_b=ids_b[0], tokens=torch.tensor(toks),
+                                 pre_logits=torch.stack(pre_logits), dec_logits=dec_logits, rec_pre=rec_pre,
+                                 conv_pre=conv_pre, rec_post=rec_post, conv_post=conv_post,
+                                 gdn_layers=torch.tensor(gdn_layers), **sd))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference-src", required=True, help="the reference project's src/ directory")
+    ap.add_argument("--only", default=None, help="generate one fixture family (e.g. engine)")
     a = ap.parse_args()
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     ref = load_reference(a.reference_src)
+    if a.only == "engine":
+        make_engine(ref, 8)
+        return
     with torch.inference_mode():
         # config 0: fp32, B=2 ragged (256, 190), 4 q/k heads x 64, 8 v heads x 64, zero initial state
         make_chunk(ref, "chunk_c0_f32.npz", [256, 190], 4, 8, 64, torch.float32, 0.0, 0)
@@ -243,6 +311,7 @@ def main():
         make_prefill_conv(ref, 5)
         make_norm(ref, 6)
         make_gates(ref, 7)
+        make_engine(ref, 8)
 
 
 if __name__ == "__main__":
