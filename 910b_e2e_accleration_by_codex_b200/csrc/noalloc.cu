@@ -4,17 +4,19 @@
 // whole device-memory budget and hands plugins only the tensors they work on, or a latency-bound
 // decode loop where cudaMalloc's implicit device synchronisation is not acceptable.  Such a
 // caller still owns every input and output, but it has no way to provide the workspace that
-// gdn_decode_layer needs between its conv kernel and its recurrence kernel.  This entry point
-// takes that workspace from a fixed-size array in device memory that belongs to the library
-// instead.
+// gdn_decode_layer needs (for dk = dv = 128 the prepared q/k/v rows and gates passed from its
+// first kernel to its second; for dk = dv = 64 the counters that order the updates of the q/k
+// conv windows shared by the value heads of one k-head).  This entry point takes that workspace
+// from a fixed-size array in device memory that belongs to the library instead.
 //
 // The array (kNoAllocScratchBytes) lives in every GPU that loads the library until the process
 // exits.  Its device address is looked up once per device, on the first call made with that
 // device current; make that first call before any stream capture.  All calls on a device share
-// the one array and it keeps whatever the last call left there: the conv kernel fully writes the
-// part a call uses before the recurrence kernel reads it, so nothing has to start at zero, but
-// two calls whose kernels overlap on the GPU (different streams, no ordering between them) race
-// on it.  Requests larger than the array are rejected with GDN_ERR_WORKSPACE; nothing here
+// the one array and it keeps whatever the last call left there.  The counters must start at
+// zero: a static device array is zero when the library loads, and every call returns each counter
+// it used to zero, so no clearing is needed between calls (the prepared rows need no clearing).
+// Two calls whose kernels overlap on the GPU (different streams, no ordering between them) race
+// on the array.  Requests larger than the array are rejected with GDN_ERR_WORKSPACE; nothing here
 // calls cudaMalloc, cudaFree or any allocating library routine.
 #include <mutex>
 
@@ -22,7 +24,7 @@
 
 namespace gdn {
 
-constexpr size_t kNoAllocScratchBytes = size_t(2) << 20;  // 2 MiB per GPU
+constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;  // 8 MiB per GPU
 constexpr int kMaxDevices = 64;
 
 static __device__ __align__(256) unsigned char g_decode_scratch[kNoAllocScratchBytes];
@@ -65,7 +67,7 @@ extern "C" int gdn_decode_layer_noalloc(const void* mixed_qkv, int64_t mixed_rs,
   if (need > kNoAllocScratchBytes)
     return fail(GDN_ERR_WORKSPACE,
                 "gdn_decode_layer_noalloc: needs %zu bytes of scratch, the built-in array holds %zu "
-                "(n * (2*Hk*dk + Hv*dv) * element size must fit)",
+                "(gdn_decode_layer_workspace_size bytes must fit)",
                 need, kNoAllocScratchBytes);
   void* scratch = nullptr;
   int rc = scratch_address(&scratch);

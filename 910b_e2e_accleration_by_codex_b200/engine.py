@@ -78,7 +78,7 @@ class CBEngine:
                     norm_w=gd.norm.weight.detach().to(bf).contiguous(),
                     eps=float(getattr(gd.norm, "variance_epsilon", getattr(gd.norm, "eps", 1e-6))))
                 ws_bytes = max(ws_bytes, ops.decode_layer_workspace_bytes(n_slots, Hk, Hv, dk, dv, bf))
-        self._ws = torch.empty(max(ws_bytes, 256), dtype=torch.uint8, device=self.dev)
+        self._ws = torch.zeros(max(ws_bytes, 256), dtype=torch.uint8, device=self.dev)  # decode tickets
         self._tok = torch.zeros(n_slots, dtype=torch.long, device=self.dev)
         self._pos = torch.zeros(n_slots, dtype=torch.long, device=self.dev)
         self._slot = torch.arange(n_slots, dtype=torch.int32, device=self.dev)

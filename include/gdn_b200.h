@@ -136,7 +136,14 @@ GDN_API int gdn_recurrent(const void* q, int64_t q_sb, int64_t q_st, const void*
  *   -> l2norm(q), l2norm(k) -> single-step recurrence on rec_pool[slot_idx]
  *   (in place) -> gated RMSNorm with gate z [n, Hv, dv] -> out [n, Hv, dv].
  *   a, b: [n, Hv] (dtype); A_log, dt_bias: [Hv] f32; norm_w: [dv] (dtype).
- * Needs a workspace of gdn_decode_layer_workspace_size() bytes (device).
+ * dk = dv = 128: two kernels per call, a prep kernel (conv, l2norm, gates)
+ * and a persistent state kernel launched as its programmatic dependent; the
+ * workspace (gdn_decode_layer_workspace_size() bytes, 16-byte aligned) carries
+ * the prepared q/k/v rows [n, C] and gates [n, Hv, 4] f32 between them.
+ * dk = dv = 64: one kernel; the workspace holds one uint32 ticket per (slot
+ * entry, k-head) that orders the updates of the q/k conv windows shared by a
+ * k-head's Hv/Hk value heads.  Zero-fill the workspace before its first use;
+ * every call leaves the tickets at zero.
  */
 GDN_API size_t gdn_decode_layer_workspace_size(int n, int Hk, int Hv, int dk, int dv, int dtype);
 
@@ -154,12 +161,13 @@ GDN_API int gdn_decode_layer(const void* mixed_qkv, int64_t mixed_rs, const void
  * separates workspace from its torch ops.  Hosts such as a serving runtime
  * that owns the whole device-memory budget, or a decode loop that cannot pay
  * cudaMalloc's implicit synchronisation, pass only inputs and outputs here; the
- * workspace is a fixed array of gdn_decode_layer_noalloc_max_bytes() (2 MiB)
+ * workspace is a fixed array of gdn_decode_layer_noalloc_max_bytes() (8 MiB)
  * inside the library, held by every GPU that loads it until exit.  Its address
  * is looked up on the first call per device (make that call before any stream
  * capture).  All calls on a device share that array: calls whose kernels
- * overlap on the GPU race.  Nothing in it has to start zeroed (each call
- * writes the part it reads).  Requests larger than the array return
+ * overlap on the GPU race.  It holds the workspace described above (the
+ * tickets are zero when the library loads, and every call leaves them zero).
+ * Requests larger than the array return
  * GDN_ERR_WORKSPACE.  Arguments as gdn_decode_layer minus the workspace.
  */
 GDN_API size_t gdn_decode_layer_noalloc_max_bytes(void);

@@ -64,7 +64,9 @@ def test_validation_errors_without_gpu(lib):
     assert rc == 2 and b"multiple" in lib.gdn_last_error()
     with pytest.raises(RuntimeError, match="status 2"):
         L.check(2, "probe")
-    assert lib.gdn_decode_layer_workspace_size(16, 16, 48, 128, 128, 1) >= 16 * 10240 * 2
+    # dk = 128: prepared q/k/v rows [n, C] bf16 + gates [n, Hv, 4] f32; dk = 64: a ticket per (slot, k-head)
+    assert lib.gdn_decode_layer_workspace_size(16, 16, 48, 128, 128, 1) == 16 * 10240 * 2 + 16 * 48 * 16
+    assert lib.gdn_decode_layer_workspace_size(16, 4, 8, 64, 64, 1) >= 16 * 4 * 4
 
 
 def test_ops_refuse_cpu_tensors():

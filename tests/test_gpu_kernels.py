@@ -297,43 +297,77 @@ def test_chunk_matches_token_recurrence_bf16(ops):
 
 
 # ----------------------------------------------------------------------------- fused decode layer
-def test_decode_layer_matches_oracle_composition(ops):
-    rng = np.random.default_rng(7)
-    n, S, Hk, Hv, dd, K = 5, 8, 2, 6, 128, 4
+def _decode_layer_case(ops, n, S, Hk, Hv, slot, steps, seed=7, conv_b=False, dd=128, K=4):
+    rng = np.random.default_rng(seed)
     Cc = 2 * Hk * dd + Hv * dd
     bf = torch.bfloat16
     r16 = lambda a: O.bf16(np.asarray(a, np.float32))
-    mixed = r16(rng.standard_normal((n, Cc)))
-    z = r16(rng.standard_normal((n, Hv, dd)))
-    a = r16(rng.standard_normal((n, Hv)))
-    b = r16(rng.standard_normal((n, Hv)))
     A_log = np.log(rng.uniform(1, 16, Hv)).astype(np.float32)
     dt_bias = rng.uniform(-1, 1, Hv).astype(np.float32)
     conv_w = r16(rng.uniform(-0.5, 0.5, (Cc, K)))
+    bias = r16(rng.uniform(-0.5, 0.5, Cc)) if conv_b else None
     conv_pool = r16(rng.standard_normal((S, Cc, K)))
     rec_pool = (rng.standard_normal((S, Hv, dd, dd)) * 0.1).astype(np.float32)
     norm_w = r16(1 + 0.1 * rng.standard_normal(dd))
-    slot = np.array([6, 1, 3, 0, 4], np.int32)
-    # oracle: elem conv -> split -> gates -> recurrence -> gated norm
-    cp = conv_pool.copy()
-    st = cp[slot]
-    y = O.conv_update_elem(mixed[:, :, None], st, conv_w, None, "bf16")[:, :, 0]
-    cp[slot] = st
-    qo, ko, vo = y[:, :Hk * dd].reshape(n, Hk, dd), y[:, Hk * dd:2 * Hk * dd].reshape(n, Hk, dd), \
-        y[:, 2 * Hk * dd:].reshape(n, Hv, dd)
-    beta, g = O.decode_gates(a, b, A_log, dt_bias, "bf16")
-    rp = rec_pool.copy()
-    core = O.decode_step_slots(qo, ko, vo, g, beta, rp, slot, True, "bf16")
-    ref = O.gated_rmsnorm(core, z, norm_w, 1e-6, "bf16")
-    # kernel
+    cp, rp = conv_pool.copy(), rec_pool.copy()
     conv_d, rec_d = T(conv_pool, bf), T(rec_pool)
-    out = ops.decode_layer(T(mixed, bf), T(z, bf), T(a, bf), T(b, bf), T(A_log), T(dt_bias), T(conv_w, bf), None,
-                           conv_d, rec_d, torch.tensor(slot, device=DEV), T(norm_w, bf), 1e-6, Hk, Hv, dd, dd)
-    assert np.array_equal(N(conv_d), cp)
-    assert bf16_ok(N(out), ref)
-    assert np.abs(N(rec_d)[slot] - rp[slot]).max() < 1e-4
+    ws = ops.decode_layer_workspace(n, Hk, Hv, dd, dd, bf, DEV)
+    slot_d = torch.tensor(slot, device=DEV)
+    for _ in range(steps):
+        mixed = r16(rng.standard_normal((n, Cc)))
+        z = r16(rng.standard_normal((n, Hv, dd)))
+        a = r16(rng.standard_normal((n, Hv)))
+        b = r16(rng.standard_normal((n, Hv)))
+        # oracle: elem conv -> split -> gates -> recurrence -> gated norm
+        st = cp[slot]
+        y = O.conv_update_elem(mixed[:, :, None], st, conv_w, bias, "bf16")[:, :, 0]
+        cp[slot] = st
+        qo, ko, vo = y[:, :Hk * dd].reshape(n, Hk, dd), y[:, Hk * dd:2 * Hk * dd].reshape(n, Hk, dd), \
+            y[:, 2 * Hk * dd:].reshape(n, Hv, dd)
+        beta, g = O.decode_gates(a, b, A_log, dt_bias, "bf16")
+        core = O.decode_step_slots(qo, ko, vo, g, beta, rp, slot, True, "bf16")
+        ref = O.gated_rmsnorm(core, z, norm_w, 1e-6, "bf16")
+        out = ops.decode_layer(T(mixed, bf), T(z, bf), T(a, bf), T(b, bf), T(A_log), T(dt_bias), T(conv_w, bf),
+                               None if bias is None else T(bias, bf), conv_d, rec_d, slot_d, T(norm_w, bf), 1e-6,
+                               Hk, Hv, dd, dd, workspace=ws)
+        assert np.array_equal(N(conv_d), cp)
+        assert bf16_ok(N(out), ref)
+        assert np.abs(N(rec_d)[slot] - rp[slot]).max() < 1e-4
     untouched = np.setdiff1d(np.arange(S), slot)
     assert np.array_equal(N(rec_d)[untouched], rec_pool[untouched])
+    assert np.array_equal(N(conv_d)[untouched], conv_pool[untouched])
+
+
+def test_decode_layer_matches_oracle_composition(ops):
+    _decode_layer_case(ops, 5, 8, 2, 6, np.array([6, 1, 3, 0, 4], np.int32), steps=1)
+
+
+def test_decode_layer_many_items_per_cta_two_steps(ops):
+    # 32 x 16 = 512 (slot, head) items: every CTA of the persistent kernel runs several of them,
+    # so each shared-memory stage is reused; two steps check the state and windows carry over
+    rng = np.random.default_rng(3)
+    slot = rng.permutation(40)[:32].astype(np.int32)
+    _decode_layer_case(ops, 32, 40, 4, 16, slot, steps=2, seed=11, conv_b=True)
+
+
+def test_decode_layer_bad_slot_sets_error_flag(ops):
+    n, S, Hk, Hv, dd, K = 3, 4, 1, 2, 128, 4
+    Cc = 2 * Hk * dd + Hv * dd
+    bf = torch.bfloat16
+    g = torch.Generator(device="cpu").manual_seed(0)
+    rnd = lambda *sh: torch.randn(*sh, generator=g).to(DEV)
+    conv_pool, rec_pool = rnd(S, Cc, K).to(bf), rnd(S, Hv, dd, dd) * 0.1
+    conv0, rec0 = conv_pool.clone(), rec_pool.clone()
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    slot = torch.tensor([2, 7, 0], dtype=torch.int32, device=DEV)      # 7 is out of range
+    ops.decode_layer(rnd(n, Cc).to(bf), rnd(n, Hv, dd).to(bf), rnd(n, Hv).to(bf), rnd(n, Hv).to(bf),
+                     torch.zeros(Hv, device=DEV), torch.zeros(Hv, device=DEV), rnd(Cc, K).to(bf), None,
+                     conv_pool, rec_pool, slot, torch.ones(dd, device=DEV).to(bf), 1e-6, Hk, Hv, dd, dd, err=err)
+    torch.cuda.synchronize()
+    assert err.item() == 1
+    for s_ in (1, 3):   # rows no valid entry points at stay bit-identical
+        assert torch.equal(conv_pool[s_], conv0[s_]) and torch.equal(rec_pool[s_], rec0[s_])
+    assert not torch.equal(rec_pool[2], rec0[2]) and not torch.equal(rec_pool[0], rec0[0])
 
 
 # ----------------------------------------------------------------------------- full config-1 size

@@ -62,7 +62,7 @@ def test_noalloc_decode_matches_workspace_entry_point_two_steps():
     n, Hk, Hv, d, K = x["dims"]
     need = lib.gdn_decode_layer_workspace_size(n, Hk, Hv, d, d, 1)
     assert need <= lib.gdn_decode_layer_noalloc_max_bytes()
-    ws = torch.empty(need, dtype=torch.uint8, device=DEV)
+    ws = torch.zeros(need, dtype=torch.uint8, device=DEV)   # the workspace starts zero-filled
     conv_a, rec_a = x["conv_pool"].clone(), x["rec_pool"].clone()
     conv_b, rec_b = x["conv_pool"].clone(), x["rec_pool"].clone()
     out_a = torch.empty(n, Hv, d, dtype=torch.bfloat16, device=DEV)
@@ -82,7 +82,9 @@ def test_noalloc_rejects_requests_beyond_its_array():
     L = pkg("_lib")
     lib = L.load()
     cap = lib.gdn_decode_layer_noalloc_max_bytes()
-    n = cap // ((2 * 16 * 128 + 48 * 128) * 2) + 1            # one slot more than fits
+    n = 1
+    while lib.gdn_decode_layer_workspace_size(n, 16, 48, 128, 128, 1) <= cap:
+        n *= 2                         # a slot count whose workspace does not fit
     rc = lib.gdn_decode_layer_noalloc(*([None, 0] + [None] * 10 + [1, None, 1e-6, None]),
                                       n, 16, 48, 128, 128, 4, 1, 1, None, None)
     assert rc == 5 and b"scratch" in lib.gdn_last_error()
