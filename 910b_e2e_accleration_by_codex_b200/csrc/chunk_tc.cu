@@ -38,6 +38,7 @@ constexpr int kNT = 384;   // warps 0-7: intra-chunk group, warps 8-11: recurren
 constexpr int kNI = 256;   // intra-group threads
 
 constexpr uint32_t TMEM_COLS = 512;
+constexpr int kSortMax = 256;  // sequences ranked by length in-kernel (beyond: index order)
 constexpr int LT = 68;   // row stride (floats) of the fp32 64x64 scratch: 16-byte aligned rows
 constexpr int LP = 36;   // row stride of the 32x32 merge scratch
 constexpr float kLog2e = 1.4426950408889634f;
@@ -225,6 +226,18 @@ struct ChunkVec {
   int pad;
 };
 
+// One (sequence, value head) work item and a chunk cursor over a CTA's work list.
+struct ItemInfo {
+  int b, h, hk, nch;
+  int64_t s0, s1, islot, fslot;
+  bool init, ok;
+};
+struct Cur {
+  int k, ci;
+  ItemInfo it;
+  bool live;
+};
+
 // shared-memory map of the warp-specialised kernel (bytes from a 1024-byte aligned base)
 constexpr uint32_t W_QK0 = 0;          // QK stage 0: [Q d0-63 | K d0-63 | Q d64-127 | K d64-127]
 constexpr uint32_t W_QK1 = 32768;      // QK stage 1
@@ -240,7 +253,8 @@ constexpr uint32_t W_BQK1 = 188416;    // buffer 1
 constexpr uint32_t W_X = 196608;       // fp32 64 x LT inverse scratch (17408 B) + 32 x LP merge scratch
 constexpr uint32_t W_VEC = 218624;     // 2 x ChunkVec
 constexpr uint32_t W_BAR = W_VEC + 2 * 2048;  // mbarriers
-constexpr uint32_t W_SMEM = W_BAR + 128 + 1024;
+constexpr uint32_t W_ORD = W_BAR + 128;  // sequences ranked longest first (kSortMax ints)
+constexpr uint32_t W_SMEM = W_ORD + 4 * 256 + 1024;
 static_assert(sizeof(ChunkVec) <= 2048, "ChunkVec");
 static_assert(W_X + 64 * LT * 4 + 32 * LP * 4 <= W_VEC, "scratch");
 
@@ -266,42 +280,89 @@ __global__ void __launch_bounds__(kNT, 1)
   const uint32_t bar_mi = smem_u32(&bars[3]), bar_mr = smem_u32(&bars[4]);
   const uint32_t bar_ready0 = smem_u32(&bars[5]), bar_free0 = smem_u32(&bars[7]);
 
-  const int h = blockIdx.x, b = blockIdx.y;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int grp = warp >= 8 ? 1 : 0;  // 0: intra-chunk group (warps 0-7), 1: recurrence group (8-11)
   const int wg = warp & 3;            // TMEM lane quarter this warp may access
   const int hv = (warp >> 2) & 1;     // intra group: which half of the columns this warp handles
   const int row = 32 * wg + lane;     // TMEM lane of this thread
   const uint32_t lane_off = uint32_t(32 * wg) << 16;
-  const int hk = h / (p.Hv / p.Hk);
   const float scale = float(1.0 / sqrt(double(kD)));
-  const int64_t s0 = p.cu[b], s1 = p.cu[b + 1];
 
-  const bool want_init = p.init_pool && (p.use_init == nullptr || p.use_init[b] != 0);
-  const int64_t islot = p.init_slot ? int64_t(p.init_slot[b]) : int64_t(b);
-  const int64_t fslot = p.final_slot ? int64_t(p.final_slot[b]) : int64_t(b);
-  if ((want_init && (islot < 0 || islot >= p.n_slots)) || (p.final_pool && (fslot < 0 || fslot >= p.n_slots))) {
-    if (tid == 0 && p.err) atomicExch(p.err, 1);
-    return;
+  // Work list.  The B * Hv (sequence, value head) items, sequences ranked longest first, are dealt
+  // to the persistent CTAs in snake order (round k gives item k * P + c, or k * P + P - 1 - c on
+  // odd rounds, to CTA c), which balances the rounds of unequal length.  Both warp groups walk the
+  // same list; the intra group runs up to two chunks ahead, across item boundaries.
+  const int P = int(gridDim.x), cta = int(blockIdx.x);
+  const int nitems = p.B * p.Hv;
+  int* ord = reinterpret_cast<int*>(sm + W_ORD);
+  const bool sorted = p.B > 1 && p.B <= kSortMax;
+  if (sorted) {
+    int* lens = reinterpret_cast<int*>(sm + W_X);  // the inverse scratch is free until the first chunk
+    for (int i = tid; i < p.B; i += kNT) lens[i] = p.cu[i + 1] - p.cu[i];
+    __syncthreads();
+    for (int i = tid; i < p.B; i += kNT) {
+      const int li = lens[i];
+      int rank = 0;
+      for (int l = 0; l < p.B; ++l) rank += (lens[l] > li) || (lens[l] == li && l < i);
+      ord[rank] = i;
+    }
+    __syncthreads();
   }
-  const int nchunks = int((s1 - s0 + kC - 1) / kC);
+  // k-th item of this CTA; false past the end of its list
+  auto item = [&](int k, ItemInfo& it) -> bool {
+    const int u = k * P + ((k & 1) ? P - 1 - cta : cta);
+    if (u >= nitems) return false;
+    const int r = u / p.Hv;
+    it.h = u - r * p.Hv;
+    it.b = sorted ? ord[r] : r;
+    it.hk = it.h / (p.Hv / p.Hk);
+    it.s0 = p.cu[it.b];
+    it.s1 = p.cu[it.b + 1];
+    it.nch = it.s1 > it.s0 ? int((it.s1 - it.s0 + kC - 1) / kC) : 0;
+    it.init = p.init_pool && (p.use_init == nullptr || p.use_init[it.b] != 0);
+    it.islot = p.init_slot ? int64_t(p.init_slot[it.b]) : int64_t(it.b);
+    it.fslot = p.final_slot ? int64_t(p.final_slot[it.b]) : int64_t(it.b);
+    it.ok = !((it.init && (it.islot < 0 || it.islot >= p.n_slots)) ||
+              (p.final_pool && (it.fslot < 0 || it.fslot >= p.n_slots)));
+    return true;
+  };
+  // chunk cursor over the items that have chunks (valid slots, non-empty)
+  auto seek = [&](Cur& x, int k) {
+    for (;; ++k) {
+      if (!item(k, x.it)) {
+        x.live = false;
+        return;
+      }
+      if (x.it.ok && x.it.nch > 0) {
+        x.k = k;
+        x.ci = 0;
+        x.live = true;
+        return;
+      }
+    }
+  };
+  auto step = [&](Cur& x) {
+    if (!x.live) return;
+    if (x.ci + 1 < x.it.nch) ++x.ci;
+    else seek(x, x.k + 1);
+  };
 
-  auto issue_qk = [&](int ci) {
-    const int st = ci & 1;
+  auto issue_qk = [&](const Cur& x, int gc) {
+    const int st = gc & 1;
     const uint32_t bar = bar_qk0 + 8 * st;
     const uint32_t qk = sb + (st ? W_QK1 : W_QK0);
-    const int c0 = int(s0) + ci * kC;
+    const int c0 = int(x.it.s0) + x.ci * kC;
     mbar_expect_tx(bar, 4 * 8192);
-    tma_load_3d(qk + 0, &tq, bar, 0, hk, c0);
-    tma_load_3d(qk + 8192, &tk, bar, 0, hk, c0);
-    tma_load_3d(qk + 16384, &tq, bar, 64, hk, c0);
-    tma_load_3d(qk + 24576, &tk, bar, 64, hk, c0);
+    tma_load_3d(qk + 0, &tq, bar, 0, x.it.hk, c0);
+    tma_load_3d(qk + 8192, &tk, bar, 0, x.it.hk, c0);
+    tma_load_3d(qk + 16384, &tq, bar, 64, x.it.hk, c0);
+    tma_load_3d(qk + 24576, &tk, bar, 64, x.it.hk, c0);
   };
-  auto issue_v = [&](int ci) {
-    const int c0 = int(s0) + ci * kC;
+  auto issue_v = [&](const Cur& x) {
+    const int c0 = int(x.it.s0) + x.ci * kC;
     mbar_expect_tx(bar_v, 2 * 8192);
-    tma_load_3d(sb + W_V, &tv, bar_v, 0, h, c0);
-    tma_load_3d(sb + W_V + 8192, &tv, bar_v, 64, h, c0);
+    tma_load_3d(sb + W_V, &tv, bar_v, 0, x.it.h, c0);
+    tma_load_3d(sb + W_V + 8192, &tv, bar_v, 64, x.it.h, c0);
   };
 
   if (tid == 0) {
@@ -310,11 +371,14 @@ __global__ void __launch_bounds__(kNT, 1)
     prefetch_tmap(&tq);
     prefetch_tmap(&tk);
     prefetch_tmap(&tv);
-    if (nchunks > 0) {
-      issue_qk(0);
-      issue_v(0);
+    Cur x;
+    seek(x, 0);
+    if (x.live) {
+      issue_qk(x, 0);
+      issue_v(x);
+      step(x);
+      if (x.live) issue_qk(x, 1);
     }
-    if (nchunks > 1) issue_qk(1);
   }
   if (warp == 0) {
     tmem_alloc(smem_u32(tmem_slot), TMEM_COLS);
@@ -330,25 +394,29 @@ __global__ void __launch_bounds__(kNT, 1)
     // ======================================================================== intra-chunk group
     uint32_t ph_mi = 0;
     float pg0 = 0.f, pg1 = 0.f, pb0 = 0.f, pb1 = 0.f;
-    auto load_gates = [&](int ci) {
-      const int64_t c0 = s0 + int64_t(ci) * kC;
-      const int t0 = 2 * lane, t1 = 2 * lane + 1;
+    auto load_gates = [&](const Cur& x) {
+      const int64_t c0 = x.it.s0 + int64_t(x.ci) * kC, s1 = x.it.s1;
+      const int t0 = 2 * lane, t1 = 2 * lane + 1, h = x.it.h;
       pg0 = c0 + t0 < s1 ? p.g[(c0 + t0) * p.gb_st + h] : 0.f;
       pg1 = c0 + t1 < s1 ? p.g[(c0 + t1) * p.gb_st + h] : 0.f;
       pb0 = c0 + t0 < s1 ? p.beta[(c0 + t0) * p.gb_st + h] : 0.f;
       pb1 = c0 + t1 < s1 ? p.beta[(c0 + t1) * p.gb_st + h] : 0.f;
     };
-    if (warp == 0 && nchunks > 0) load_gates(0);
-    for (int ci = 0; ci < nchunks; ++ci) {
-      const int bf = ci & 1;
+    Cur cur, nx;
+    seek(cur, 0);
+    nx = cur;
+    step(nx);
+    if (warp == 0 && cur.live) load_gates(cur);
+    for (int gc = 0; cur.live; ++gc) {
+      const int bf = gc & 1;
       ChunkVec& cv = *reinterpret_cast<ChunkVec*>(sm + W_VEC + 2048 * bf);
-      const int64_t c0 = s0 + int64_t(ci) * kC;
+      const int64_t c0 = cur.it.s0 + int64_t(cur.ci) * kC, s1 = cur.it.s1;
       const int nt = int((s1 - c0) < kC ? (s1 - c0) : kC);
       uint8_t* qk = sm + (bf ? W_QK1 : W_QK0);
       const uint32_t qk_a = sb + (bf ? W_QK1 : W_QK0);
       const uint32_t bqk = bf ? W_BQK1 : W_BQK0;
-      // chunk ci-2 has left this buffer set (vectors, QKm tile, TMEM U/W buffers)
-      if (ci >= 2 && ok && !mbar_wait(bar_free0 + 8 * bf, uint32_t((ci - 2) >> 1) & 1u)) ok = false;
+      // chunk gc-2 has left this buffer set (vectors, QKm tile, TMEM U/W buffers)
+      if (gc >= 2 && ok && !mbar_wait(bar_free0 + 8 * bf, uint32_t((gc - 2) >> 1) & 1u)) ok = false;
       tc_fence_after();
       if (warp == 0) {  // gates: gc = cumsum(g) (log2-scaled), beta; prefetch the next chunk's
         const int t0 = 2 * lane, t1 = 2 * lane + 1;
@@ -373,9 +441,9 @@ __global__ void __launch_bounds__(kNT, 1)
           cv.Gl = ex2(gl);
           cv.nt = nt;
         }
-        if (ci + 1 < nchunks) load_gates(ci + 1);
+        if (nx.live) load_gates(nx);
       }
-      if (ok && !mbar_wait(bar_qk0 + 8 * bf, uint32_t(ci >> 1) & 1u)) ok = false;
+      if (ok && !mbar_wait(bar_qk0 + 8 * bf, uint32_t(gc >> 1) & 1u)) ok = false;
       if (nt < kC) {  // zero the q/k rows past the sequence end (they hold the next sequence)
         for (int i = tid; i < (kC - nt) * 32; i += kNI) {
           const int r = nt + (i >> 5), tile = (i >> 3) & 3, cc = i & 7;
@@ -456,7 +524,7 @@ __global__ void __launch_bounds__(kNT, 1)
         store_row16(sm + W_BU, 64, t, cb >> 3, u);
         store_row16(sm + W_BW, 64, t, cb >> 3, w);
       }
-      if (ok && !mbar_wait(bar_v, uint32_t(ci) & 1u)) ok = false;
+      if (ok && !mbar_wait(bar_v, uint32_t(gc) & 1u)) ok = false;
       if (nt < kC) {
         for (int i = tid; i < (kC - nt) * 16; i += kNI) {
           const int r = nt + (i >> 4), tile = (i >> 3) & 1, cc = i & 7;
@@ -483,23 +551,37 @@ __global__ void __launch_bounds__(kNT, 1)
       tc_fence_before();
       group_sync(1);
       if (tid == 0) {
-        if (ci + 1 < nchunks) {  // the V buffer is free: fetch the next chunk's
+        if (nx.live) {  // the V buffer is free: fetch the next chunk's
           fence_async_smem();
-          issue_v(ci + 1);
+          issue_v(nx);
         }
-        mbar_arrive(bar_ready0 + 8 * bf);  // hand chunk ci to the recurrence group
+        mbar_arrive(bar_ready0 + 8 * bf);  // hand chunk gc to the recurrence group
       }
+      cur = nx;
+      step(nx);
     }
   } else {
     // ======================================================================== recurrence group
     const int rt = tid - kNI;
     uint32_t ph_mr = 0;
+    Cur q2;  // the chunk two ahead of the current one (its Q/K tiles are fetched into the freed stage)
+    seek(q2, 0);
+    step(q2);
+    step(q2);
+    int gc = 0;
+    ItemInfo itm;
+    for (int k = 0; item(k, itm); ++k) {
+    if (!itm.ok) {  // a bad slot index: record it and leave every pool row untouched
+      if (rt == 0 && p.err) atomicExch(p.err, 1);
+      continue;
+    }
+    const int h = itm.h;
     {  // initial state -> TMEM (thread: row k, all 128 columns)
       float v[32];
 #pragma unroll
       for (int part = 0; part < 4; ++part) {
-        if (want_init) {
-          const float4* src = reinterpret_cast<const float4*>(p.init_pool + (islot * p.Hv + h) * int64_t(kD * kD) +
+        if (itm.init) {
+          const float4* src = reinterpret_cast<const float4*>(p.init_pool + (itm.islot * p.Hv + h) * int64_t(kD * kD) +
                                                               int64_t(row) * kD + 32 * part);
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
@@ -514,14 +596,14 @@ __global__ void __launch_bounds__(kNT, 1)
       }
       tmem_st_wait();
     }
-    for (int ci = 0; ci < nchunks; ++ci) {
-      const int bf = ci & 1;
+    for (int ci = 0; ci < itm.nch; ++ci, ++gc) {
+      const int bf = gc & 1;
       const ChunkVec& cv = *reinterpret_cast<const ChunkVec*>(sm + W_VEC + 2048 * bf);
-      const int64_t c0 = s0 + int64_t(ci) * kC;
+      const int64_t c0 = itm.s0 + int64_t(ci) * kC;
       const uint32_t qk_a = sb + (bf ? W_QK1 : W_QK0);
       const uint32_t bqk = bf ? W_BQK1 : W_BQK0;
       const uint32_t tU = tmem + T_U0 + 64 * bf, tW = tmem + T_W0 + 64 * bf;
-      if (ok && !mbar_wait(bar_ready0 + 8 * bf, uint32_t(ci >> 1) & 1u)) ok = false;
+      if (ok && !mbar_wait(bar_ready0 + 8 * bf, uint32_t(gc >> 1) & 1u)) ok = false;
       tc_fence_after();
       if (rt == 0) bulk_wait_read();  // the previous chunk's output store has left W_WT
       group_sync(2);
@@ -623,13 +705,14 @@ __global__ void __launch_bounds__(kNT, 1)
         }
       }
       group_sync(2);
-      if (rt == 0) {  // chunk ci is done with its buffer set: prefetch chunk ci+2 into it, free it
-        if (ci + 2 < nchunks) {
+      if (rt == 0) {  // chunk gc is done with its buffer set: prefetch chunk gc+2 into it, free it
+        if (q2.live) {
           fence_async_smem();
-          issue_qk(ci + 2);
+          issue_qk(q2, gc + 2);
         }
         mbar_arrive(bar_free0 + 8 * bf);
       }
+      step(q2);
     }
     // final state
     if (p.final_pool) {
@@ -637,11 +720,12 @@ __global__ void __launch_bounds__(kNT, 1)
       for (int part = 0; part < 4; ++part) {
         float v[32];
         tmem_ld32(tmem + T_S + lane_off + 32 * part, v);
-        float4* dst = reinterpret_cast<float4*>(p.final_pool + (fslot * p.Hv + h) * int64_t(kD * kD) +
+        float4* dst = reinterpret_cast<float4*>(p.final_pool + (itm.fslot * p.Hv + h) * int64_t(kD * kD) +
                                                 int64_t(row) * kD + 32 * part);
 #pragma unroll
         for (int i = 0; i < 8; ++i) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
       }
+    }
     }
     if (rt == 0) bulk_wait_all();
   }
@@ -706,15 +790,26 @@ int run_chunk_tc(const ChunkParams& p, int64_t T_total, cudaStream_t s) {
   if (use_store && make_map(&mo, p.out, p.Hv, T_total, p.o_st, true) != GDN_OK) use_store = 0;
   if (!use_store) mo = mq;  // never read
   static bool attr_set[64] = {};
+  static int sm_count[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+  int sms = 148;
+  if (dev >= 0 && dev < 64 && attr_set[dev]) {
+    sms = sm_count[dev];
+  } else {
     cudaError_t e = cudaFuncSetAttribute(chunk_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          int(W_SMEM));
-    if (e != cudaSuccess) return fail(GDN_ERR_CUDA, "chunk_tc: smem attribute: %s", cudaGetErrorString(e));
-    if (dev >= 0 && dev < 64) attr_set[dev] = true;
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return fail(GDN_ERR_CUDA, "chunk_tc: setup: %s", cudaGetErrorString(e));
+    if (dev >= 0 && dev < 64) {
+      sm_count[dev] = sms;
+      attr_set[dev] = true;
+    }
   }
-  chunk_tc_kernel<<<dim3(p.Hv, p.B), kNT, W_SMEM, s>>>(p, mq, mk, mv, mo, use_store);
+  // persistent: one CTA per SM walks its share of the (sequence, head) items
+  const int64_t items = int64_t(p.B) * p.Hv;
+  if (items > (int64_t(1) << 30)) return fail(GDN_ERR_ARG, "gdn_chunk_prefill: B * Hv too large");
+  chunk_tc_kernel<<<dim3(unsigned(items < sms ? items : sms)), kNT, W_SMEM, s>>>(p, mq, mk, mv, mo, use_store);
   return check_launch("gdn_chunk_prefill (tensor cores)");
 }
 
