@@ -36,6 +36,8 @@ constexpr int kC = 64;
 constexpr int kD = 128;
 constexpr int kNT = 384;   // warps 0-7: intra-chunk group, warps 8-11: recurrence group
 constexpr int kNI = 256;   // intra-group threads
+constexpr int kRegLaunch = 168, kRegIntra = 136, kRegRec = 232;  // setmaxnreg split (see the kernel)
+static_assert(2 * 128 * kRegIntra + 128 * kRegRec == kNT * kRegLaunch, "register split must match the launch");
 
 constexpr uint32_t TMEM_COLS = 512;
 constexpr int kSortMax = 256;  // sequences ranked by length in-kernel (beyond: index order)
@@ -125,15 +127,25 @@ __device__ __forceinline__ void tri_inverse64(float* X, float* P, int warp, int 
     for (int i = 0; i < 16; ++i) acc[i] = lds1(X + (b0 + i) * LT + b0 + j);
 #pragma unroll
     for (int mg = 0; mg < 4; ++mg) {
-      float4 xr[16];
+      // the 4 x 4 triangle of columns 4mg..4mg+3 resolves r[4mg..4mg+3] ...
+      float4 xt[4];
 #pragma unroll
-      for (int i = 0; i < 16; ++i) xr[i] = lds4(X + (b0 + i) * LT + b0 + 4 * mg);
+      for (int u = 0; u < 4; ++u) xt[u] = lds4(X + (b0 + 4 * mg + u) * LT + b0 + 4 * mg);
 #pragma unroll
       for (int mm = 0; mm < 4; ++mm) {
         const int m = 4 * mg + mm;
         r[m] = m > j ? acc[m] : 0.f;
 #pragma unroll
-        for (int i = m + 1; i < 16; ++i) acc[i] = fmaf(f4get(xr[i], mm), r[m], acc[i]);
+        for (int u = mm + 1; u < 4; ++u) acc[4 * mg + u] = fmaf(f4get(xt[u], mm), r[m], acc[4 * mg + u]);
+      }
+      // ... which then update the rows below it, one row at a time (same FMA order per row)
+#pragma unroll
+      for (int i = 4 * mg + 4; i < 16; ++i) {
+        const float4 x = lds4(X + (b0 + i) * LT + b0 + 4 * mg);
+        acc[i] = fmaf(x.x, r[4 * mg], acc[i]);
+        acc[i] = fmaf(x.y, r[4 * mg + 1], acc[i]);
+        acc[i] = fmaf(x.z, r[4 * mg + 2], acc[i]);
+        acc[i] = fmaf(x.w, r[4 * mg + 3], acc[i]);
       }
     }
     __syncwarp();
@@ -390,6 +402,11 @@ __global__ void __launch_bounds__(kNT, 1)
   const uint32_t tmem = *tmem_slot;
   bool ok = true;
 
+  // Register split: the recurrence group's epilogues hold several 32-column TMEM rows at once, the
+  // intra group needs far fewer.  Launch: 384 threads x 168 = 64512 registers; intra 2 warpgroups x
+  // 128 x 136 = 34816 plus recurrence 128 x 232 = 29696 is exactly that.
+  if (grp == 0) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegIntra));
+  else asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegRec));
   if (grp == 0) {
     // ======================================================================== intra-chunk group
     uint32_t ph_mi = 0;
