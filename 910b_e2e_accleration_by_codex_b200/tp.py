@@ -42,8 +42,8 @@ def _set_weight(lin, w):
     lin.out_features, lin.in_features = w.shape[0], w.shape[1]
 
 
-def _rows(start, count):
-    return torch.arange(start, start + count)
+def _rows(start, count, device):
+    return torch.arange(start, start + count, device=device)
 
 
 def attention_head_split(nh, kvh, tp, rank):
@@ -97,17 +97,18 @@ def shard_model(model, rank, tp):
             kh_l, vh_l = kh // tp, vh // tp
             key_dim = gd.key_dim
             # in_proj_qkv rows: [q (kh*dk) | k (kh*dk) | v (vh*dv)]; the same head blocks in each part
-            idx = torch.cat([_rows(rank * kh_l * dk, kh_l * dk), _rows(key_dim + rank * kh_l * dk, kh_l * dk),
-                             _rows(2 * key_dim + rank * vh_l * dv, vh_l * dv)])
+            dev = gd.in_proj_qkv.weight.device
+            idx = torch.cat([_rows(rank * kh_l * dk, kh_l * dk, dev), _rows(key_dim + rank * kh_l * dk, kh_l * dk, dev),
+                             _rows(2 * key_dim + rank * vh_l * dv, vh_l * dv, dev)])
             _set_weight(gd.in_proj_qkv, gd.in_proj_qkv.weight.index_select(0, idx))
             gd.conv1d.weight = nn.Parameter(gd.conv1d.weight.index_select(0, idx).contiguous(), requires_grad=False)
             if gd.conv1d.bias is not None:
                 gd.conv1d.bias = nn.Parameter(gd.conv1d.bias.index_select(0, idx).contiguous(), requires_grad=False)
             gd.conv1d.out_channels = gd.conv1d.in_channels = idx.numel()
             gd.conv1d.groups = idx.numel()
-            vrows = _rows(rank * vh_l * dv, vh_l * dv)
+            vrows = _rows(rank * vh_l * dv, vh_l * dv, dev)
             _set_weight(gd.in_proj_z, gd.in_proj_z.weight.index_select(0, vrows))
-            hrows = _rows(rank * vh_l, vh_l)
+            hrows = _rows(rank * vh_l, vh_l, dev)
             _set_weight(gd.in_proj_b, gd.in_proj_b.weight.index_select(0, hrows))
             _set_weight(gd.in_proj_a, gd.in_proj_a.weight.index_select(0, hrows))
             gd.A_log = nn.Parameter(gd.A_log.data[hrows].contiguous(), requires_grad=False)

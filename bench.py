@@ -18,6 +18,12 @@ port) on this host's cores over a bounded sample of the same workload.
 
 Multi-GPU (torchrun, one rank per GPU): every rank runs its own replica of the workload
 (weak scaling, no collective on the data path); value = all ranks' tokens / max rank time.
+
+Also reported (``model``, BASELINE configs 3/4; ``--no-model`` skips it): the ~27B hybrid (64 layers,
+3 GDN : 1 attention, hidden 5120) with random bf16 weights run through the slot engine -- one
+packed prefill of the slots' prompts (lengths U[300,700], random token ids), then graph-replayed
+decode steps for every slot; with N ranks the model is head-sharded over all of them (TP = N,
+NCCL all-reduce after o_proj/out_proj/down_proj) with min(64, 16 N) slots (64 at N = 8).
 """
 from __future__ import annotations
 
@@ -47,6 +53,15 @@ FLOP_PER_HEAD_CHUNK = 2 * CHUNK * CHUNK * D * 5 + 2 * CHUNK * D * D * 3 + 2 * CH
 # decode config 2
 DEC_LAYERS, DEC_SLOTS, CONV_K = 48, 16, 4
 CONV_DIM = 2 * HK * D + HV * D
+# model configs 3/4: ~27B hybrid (48 GDN layers of config-1 shape + 16 GQA attention layers)
+MODEL_TEXT_CONFIG = dict(
+    vocab_size=248320, hidden_size=5120, intermediate_size=17408, num_hidden_layers=64,
+    num_attention_heads=24, num_key_value_heads=4, head_dim=256, linear_num_key_heads=HK,
+    linear_num_value_heads=HV, linear_key_head_dim=D, linear_value_head_dim=D, linear_conv_kernel_dim=CONV_K,
+    layer_types=["linear_attention", "linear_attention", "linear_attention", "full_attention"] * 16,
+    max_position_embeddings=8192, rms_norm_eps=1e-6, attention_bias=False, hidden_act="silu")
+MODEL_VISION_CONFIG = dict(depth=1, hidden_size=32, num_heads=2, intermediate_size=64, out_hidden_size=5120)
+MODEL_PLEN = (300, 700)
 
 
 def parse():
@@ -60,6 +75,10 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="target CPU-baseline sample time")
+    ap.add_argument("--no-model", action="store_true",
+                    help="skip the config 3/4 model leg (the ~27B hybrid with random weights through the engine, "
+                         "tensor-parallel over all ranks when launched with more than one)")
+    ap.add_argument("--model-steps", type=int, default=32, help="timed decode steps of the model leg")
     return ap.parse_args()
 
 
@@ -338,6 +357,11 @@ def run_ours(args, world, rank, local):
     if decode is not None:
         line["decode"] = decode
         line["gpu_launches"] += decode["gpu_launches"]
+    if not args.no_model:
+        try:
+            line["model"] = run_model(args, world, rank, local)
+        except Exception as e:  # the headline stands on its own; report why the model leg is missing
+            line["model"] = {"error": f"{type(e).__name__}: {e}"[:300]}
     if rank == 0 and world == 1 and not args.no_cpu:
         torch.set_num_threads(cpu_cores())
         v_cpu, sample, el = cpu_prefill_sample(w, args.cpu_seconds)
@@ -345,6 +369,77 @@ def run_ours(args, world, rank, local):
                                 "sample": sample + f", {el:.1f} s"}
     if rank == 0:
         print(json.dumps(line), flush=True)
+
+
+def model_slots(world):
+    """Slot count of the model leg: 16 on one GPU; with TP over N ranks min(64, 16 N), 64 at N = 8."""
+    return 16 if world <= 1 else min(64, 16 * world)
+
+
+def run_model(args, world, rank, local):
+    """Model leg (configs 3/4): random-init ~27B hybrid through the slot engine."""
+    from transformers.models.qwen3_5.configuration_qwen3_5 import Qwen3_5Config
+    from transformers.models.qwen3_5.modeling_qwen3_5 import Qwen3_5ForConditionalGeneration
+    eng_mod = importlib.import_module(f"{PKG}.engine")
+    tp_mod = importlib.import_module(f"{PKG}.tp")
+    dev = torch.device("cuda", local)
+    t_build = time.time()
+    torch.manual_seed(1234)                     # identical full model on every rank before sharding
+    cfg = Qwen3_5Config(text_config=MODEL_TEXT_CONFIG, vision_config=MODEL_VISION_CONFIG)
+    prev = torch.get_default_dtype()
+    torch.set_default_dtype(torch.bfloat16)
+    try:
+        with torch.device(dev):
+            model = Qwen3_5ForConditionalGeneration(cfg)
+    finally:
+        torch.set_default_dtype(prev)
+    model = model.to(torch.bfloat16).eval()
+    params = sum(p.numel() for n, p in model.named_parameters() if "visual" not in n)
+    if world > 1:
+        tp_mod.shard_model(model, rank, world)
+    torch.cuda.empty_cache()
+    slots = model_slots(world)
+    t_max = 1024
+    eng = (tp_mod.TPEngine(model, slots, t_max, dev, world, graph_decode=True) if world > 1 else
+           eng_mod.CBEngine(model, slots, t_max, dev, graph_decode=True))
+    g = torch.Generator(device="cpu").manual_seed(4321)
+    lens = torch.randint(MODEL_PLEN[0], MODEL_PLEN[1] + 1, (slots,), generator=g).tolist()
+    prompts = [torch.randint(0, MODEL_TEXT_CONFIG["vocab_size"], (1, L), generator=g) for L in lens]
+    build_s = time.time() - t_build
+    # warm-up prefill (cuBLAS heuristics, allocator), then the timed packed prefill of every slot
+    eng.prefill_batch([0], [prompts[0][:, :64]])
+    eng.free(0)
+    torch.cuda.synchronize()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    toks = eng.prefill_batch(list(range(slots)), prompts)
+    e1.record()
+    torch.cuda.synchronize()
+    pre_ms = allreduce_max(e0.elapsed_time(e1), world)
+    all_slots = list(range(slots))
+    for _ in range(max(3, args.warmup)):
+        toks = eng.decode_step(all_slots, toks)
+    torch.cuda.synchronize()
+    barrier(world)
+    e0.record()
+    for _ in range(args.model_steps):
+        toks = eng.decode_step(all_slots, toks)
+    e1.record()
+    torch.cuda.synchronize()
+    dec_ms = allreduce_max(e0.elapsed_time(e1), world) / args.model_steps
+    eng._graphs.clear()                          # graphs holding NCCL calls go before the process group
+    eng._graph_out.clear()
+    del eng, model
+    torch.cuda.empty_cache()
+    n_pre = sum(lens)
+    return {"config": "config 3" if world <= 1 else f"config 4 (TP {world})",
+            "params": params, "layers": MODEL_TEXT_CONFIG["num_hidden_layers"], "tp": world, "slots": slots,
+            "prefill_tokens": n_pre, "prefill_ms": pre_ms, "prefill_tokens_per_s": n_pre / (pre_ms / 1e3),
+            "decode_steps": args.model_steps, "decode_ms_per_step": dec_ms,
+            "decode_tokens_per_s": slots / (dec_ms / 1e3), "graph": True, "weights": "random-init bf16",
+            "prompts": f"uniform random token ids, lengths U[{MODEL_PLEN[0]},{MODEL_PLEN[1]}]",
+            "build_s": build_s}
 
 
 def run_e2e(ops, w, q, k, v, g, beta, cu, pool, slot, use_init, out, args, world, stream, tot_tokens):
