@@ -203,24 +203,60 @@ def allreduce_sum(x: float, world: int) -> float:
 
 # ----------------------------------------------------------------------------- CPU legs
 def cpu_prefill_sample(w, seconds: float):
-    """Run the oracle (CPU restatement of src/gdn_chunk_fast2.py, one sequence per call as
-    TPEngine.prefill does) over the workload's sequences in order until ~`seconds` elapse."""
-    from oracle import gdn_oracle as O
+    """The reference's prefill path on the host cores: the torch restatement (oracle/gdn_torch_cpu.py)
+    of fast_chunk_gated_delta_rule_v2 (src/gdn_chunk_fast2.py:11-62) in the reference's dtypes, one
+    sequence per call as TPEngine.prefill does, over the workload's sequences in order until
+    ~`seconds` elapse."""
+    from oracle import gdn_torch_cpu as TC
     r = HV // HK
     toks, used, el = 0, 0, 0.0
     t0 = time.perf_counter()
-    for b, L in enumerate(w["lens"]):
-        s, e = int(w["cu"][b]), int(w["cu"][b + 1])
-        q = O.repeat_heads(w["q"][s:e].float().numpy(), r)[None]
-        k = O.repeat_heads(w["k"][s:e].float().numpy(), r)[None]
-        O.chunk_gated_delta_rule(q, k, w["v"][s:e].float().numpy()[None], w["g"][s:e].numpy()[None],
-                                 w["beta"][s:e].numpy()[None], 64, w["init"][b].numpy()[None], True, True, "bf16")
-        toks += L
-        used += 1
-        el = time.perf_counter() - t0
-        if el >= seconds:
-            break
-    return toks / el, f"{used} of {len(w['lens'])} sequences ({toks} tokens), one oracle call per sequence", el
+    with torch.inference_mode():
+        for b, L in enumerate(w["lens"]):
+            s, e = int(w["cu"][b]), int(w["cu"][b + 1])
+            q = w["q"][s:e].repeat_interleave(r, dim=1)[None]
+            k = w["k"][s:e].repeat_interleave(r, dim=1)[None]
+            TC.chunk_gated_delta_rule(q, k, w["v"][s:e][None], w["g"][s:e][None],
+                                      w["beta"][s:e].to(torch.bfloat16)[None], 64, w["init"][b][None], True, True)
+            toks += L
+            used += 1
+            el = time.perf_counter() - t0
+            if el >= seconds:
+                break
+    return toks / el, (f"{used} of {len(w['lens'])} sequences ({toks} tokens), one call per sequence of the torch "
+                       f"restatement of src/gdn_chunk_fast2.py"), el
+
+
+def cpu_decode_sample(seconds: float):
+    """The reference's decode layer on the host cores: the torch restatement (oracle/gdn_torch_cpu.py)
+    of CBEngine._gdn's operators (src/cb_engine.py:318-352: elem conv update, split, gates, l2norm,
+    recurrent_single_step with index_select / index_copy_ on the pools, gated RMSNorm) for 16 slots,
+    repeated over fresh layers until ~`seconds` elapse; returns µs per 48-layer step."""
+    from oracle import gdn_torch_cpu as TC
+    g = torch.Generator(device="cpu").manual_seed(1234)
+    n, bf = DEC_SLOTS, torch.bfloat16
+    layers, el = 0, 0.0
+    t0 = time.perf_counter()
+    with torch.inference_mode():
+        while True:
+            mixed = torch.randn(n, CONV_DIM, generator=g).to(bf)
+            z = torch.randn(n, HV, D, generator=g).to(bf)
+            a, b = torch.randn(n, HV, generator=g).to(bf), torch.randn(n, HV, generator=g).to(bf)
+            A_log = torch.log(torch.empty(HV).uniform_(1, 16, generator=g))
+            dt_bias = torch.rand(HV, generator=g) * 2 - 1
+            conv_w = (torch.rand(CONV_DIM, CONV_K, generator=g) - 0.5).to(bf)
+            conv_pool = torch.randn(n, CONV_DIM, CONV_K, generator=g).to(bf)
+            rec_pool = torch.randn(n, HV, D, D, generator=g) * 0.02
+            norm_w = (1 + 0.1 * torch.randn(D, generator=g)).to(bf)
+            slot = torch.randperm(n, generator=g)
+            t_l = time.perf_counter()
+            TC.decode_layer(mixed, z, a, b, A_log, dt_bias, conv_w, conv_pool, rec_pool, slot, norm_w, HK, HV, D)
+            el += time.perf_counter() - t_l
+            layers += 1
+            if time.perf_counter() - t0 >= seconds:
+                break
+    return el / layers * DEC_LAYERS * 1e6, (f"{layers} layers of 16 slots of the torch restatement of "
+                                            f"src/cb_engine.py:318-352, timed per layer, x {DEC_LAYERS}")
 
 
 def cpu_cores() -> int:
@@ -231,7 +267,7 @@ def cpu_cores() -> int:
 
 
 def run_reference(args, world, rank):
-    """--impl reference: the oracle port of the reference's torch path on the host cores."""
+    """--impl reference: the reference's torch path, restated (oracle/gdn_torch_cpu.py), on the host cores."""
     if rank != 0:
         return
     w = make_prefill_workload(args.seed)
@@ -367,6 +403,10 @@ def run_ours(args, world, rank, local):
         v_cpu, sample, el = cpu_prefill_sample(w, args.cpu_seconds)
         line["cpu_baseline"] = {"value": v_cpu, "unit": "tokens/s", "cores": cpu_cores(), "kind": "port",
                                 "sample": sample + f", {el:.1f} s"}
+        if decode is not None:
+            us_cpu, dsample = cpu_decode_sample(max(2.0, args.cpu_seconds / 3))
+            line["decode"]["cpu_baseline"] = {"us_per_step": us_cpu, "cores": cpu_cores(), "kind": "port",
+                                              "sample": dsample}
     if rank == 0:
         print(json.dumps(line), flush=True)
 
