@@ -13,6 +13,7 @@
 //   whole 512-byte state rows (fully coalesced).  Reductions over dk go through shared memory.
 //   The slot index is resolved in-kernel: the CTA loads pool[init_slot[b]] and stores
 //   pool[final_slot[b]] -- no index_select / index_copy_ around the call.
+#include <cstddef>
 #include <type_traits>
 
 #include "common.cuh"
@@ -385,6 +386,10 @@ struct Smem {
   float snorm[4];
   unsigned long long full[kStages];
 };
+
+static_assert(offsetof(Smem, red) % 16 == 0 && offsetof(Smem, sdelta) % 16 == 0 && offsetof(Smem, in) % 16 == 0,
+              "float4 rows and bulk-copy targets on 16-byte offsets");
+static_assert(offsetof(Smem, full) % 8 == 0, "mbarriers on 8-byte offsets");
 
 __device__ __forceinline__ void cta_sync() { asm volatile("bar.sync 1, 512;" ::: "memory"); }
 __device__ __forceinline__ void out_sync() { asm volatile("bar.sync 2, 128;" ::: "memory"); }

@@ -350,6 +350,14 @@ def test_decode_layer_many_items_per_cta_two_steps(ops):
     _decode_layer_case(ops, 32, 40, 4, 16, slot, steps=2, seed=11, conv_b=True)
 
 
+def test_decode_layer_large_batch(ops):
+    # 20 x 48 = 960 (slot, head) items: 7 per persistent CTA, so every stage of the state ring is
+    # reused at least twice
+    rng = np.random.default_rng(9)
+    slot = rng.permutation(24)[:20].astype(np.int32)
+    _decode_layer_case(ops, 20, 24, 16, 48, slot, steps=1, seed=13)
+
+
 def test_decode_layer_bad_slot_sets_error_flag(ops):
     n, S, Hk, Hv, dd, K = 3, 4, 1, 2, 128, 4
     Cc = 2 * Hk * dd + Hv * dd
