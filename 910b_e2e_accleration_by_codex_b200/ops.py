@@ -280,22 +280,25 @@ def prefill_conv_varlen(x, cu_seqlens, weight, bias=None, conv_pool=None, slot_i
 
 # ============================================================================ fused decode layer
 def decode_layer_workspace_bytes(n, Hk, Hv, dk, dv, dtype) -> int:
-    """Bytes of device workspace ``decode_layer`` needs (one uint32 ticket counter per slot entry and k-head)."""
+    """Bytes of device workspace ``decode_layer`` needs: for d = 128 the prepared q/k/v rows and gates
+    passed from its prep kernel to its state kernel; for d = 64 one uint32 ticket counter per slot
+    entry and k-head."""
     return int(_lib.load().gdn_decode_layer_workspace_size(n, Hk, Hv, dk, dv, _DT[dtype]))
 
 
 def decode_layer_workspace(n, Hk, Hv, dk, dv, dtype, device):
-    """Device workspace for ``decode_layer``: zero-filled, as the kernel requires on first use (it
-    leaves it zero-filled, so one workspace serves any number of calls)."""
+    """Device workspace for ``decode_layer``, zero-filled: the d = 64 form's ticket counters must
+    start at zero and every call leaves them at zero; the d = 128 form overwrites its rows on every
+    call.  One workspace serves any number of calls on one stream."""
     return torch.zeros(decode_layer_workspace_bytes(n, Hk, Hv, dk, dv, dtype), dtype=torch.uint8, device=device)
 
 
 def decode_layer(mixed_qkv, z, a, b, A_log, dt_bias, conv_w, conv_b, conv_pool, rec_pool, slot_idx, norm_w,
                  eps, Hk, Hv, dk, dv, conv_mode=GDN_CONV_ELEM, workspace=None, out=None, err=None):
-    """The operator part of CBEngine._gdn (src/cb_engine.py:318-352) for n slots in one kernel:
-    conv update (conv_pool[slot_idx] in place) -> gates -> l2norm -> recurrence
-    (rec_pool[slot_idx] in place) -> gated RMSNorm.  ``workspace`` (see decode_layer_workspace)
-    must be zero-filled before its first use.  mixed_qkv [n,C], z [n,Hv,dv], a/b [n,Hv],
+    """The operator part of CBEngine._gdn (src/cb_engine.py:318-352) for n slots: conv update
+    (conv_pool[slot_idx] in place) -> gates -> l2norm -> recurrence (rec_pool[slot_idx] in place)
+    -> gated RMSNorm, as a prep kernel plus a persistent state kernel (d = 128) or one kernel
+    (d = 64).  ``workspace`` (see decode_layer_workspace) must be zero-filled before its first use.  mixed_qkv [n,C], z [n,Hv,dv], a/b [n,Hv],
     A_log/dt_bias [Hv] fp32.  Returns out [n,Hv,dv]."""
     _need_cuda(mixed_qkv, z, a, b, A_log, dt_bias, conv_w, conv_pool, rec_pool, slot_idx, norm_w)
     n, Cc = mixed_qkv.shape[0], mixed_qkv.shape[-1]
