@@ -356,7 +356,7 @@ __global__ void __launch_bounds__(RecShape<DK, DV>::NT, 2) recurrent_kernel(RecP
 //                        rows in the activation dtype, the gates; writes compact rows
 //                        prep [n, C] (dtype) and gates [n, Hv, 4] f32 = (g, beta, -, -).
 //   decode_state_kernel  one CTA per SM over the items (b, h) = it, it + grid, ...: every input
-//                        of an item (its 64 KiB state, the q/k/v rows, the gates) arrives by bulk
+//                        of an item (its 64 KiB state, the q/k/v rows, the gates, the z row) arrives by bulk
 //                        copy (cp.async.bulk on the stage's mbarrier) into a 3-deep shared-memory
 //                        ring, issued by one thread two items ahead; the compute warps write the
 //                        new state back into its stage and the same thread stores it with a bulk
@@ -372,10 +372,10 @@ constexpr int kStages = 3;
 constexpr int kThreads = 512;               // 16 warps; warp w owns state rows w, w+16, ..., lane 4 columns
 constexpr int kRows = D / 16;
 constexpr int kOutTid0 = 3 * D;             // warps 12-15 produce the output of the previous item
-constexpr int kCopyTid = 3 * D + 96;        // issues the bulk loads and stores
+constexpr int kCopyTid = 11 * 32;           // issues the bulk loads and stores (not an output warp)
 constexpr int kSlotCache = 512;             // slot indices of a CTA's first items kept in shared memory
 constexpr uint32_t kStateBytes = D * D * 4;
-constexpr int kInFloats = 4 + 3 * D;        // per stage: gates (4 floats), then q, k, v rows (up to f32)
+constexpr int kInFloats = 4 + 4 * D;        // per stage: gates (4 floats), then q, k, v, z rows (up to f32)
 
 struct Smem {
   float state[kStages][D * D];
@@ -459,7 +459,7 @@ __global__ void __launch_bounds__(dec::kThreads, 1) decode_state_kernel(RecParam
   const int grid = gridDim.x;
   const int nmine = nitems > int(blockIdx.x) ? (nitems - int(blockIdx.x) + grid - 1) / grid : 0;
   constexpr uint32_t kRowBytes = D * sizeof(T);
-  constexpr uint32_t kStageTx = kStateBytes + 16 + 3 * kRowBytes;
+  constexpr uint32_t kStageTx = kStateBytes + 16 + 4 * kRowBytes;
 
   if (tid == 0) {
     for (int k = 0; k < kStages; ++k) mbar_init(smem_u32(&sm.full[k]), 1);
@@ -500,6 +500,7 @@ __global__ void __launch_bounds__(dec::kThreads, 1) decode_state_kernel(RecParam
     bulk_load(dst + 16, row + hk * D, kRowBytes, bar);
     bulk_load(dst + 16 + kRowBytes, row + (p.Hk + hk) * D, kRowBytes, bar);
     bulk_load(dst + 16 + 2 * kRowBytes, row + (2 * p.Hk + h) * D, kRowBytes, bar);
+    bulk_load(dst + 16 + 3 * kRowBytes, reinterpret_cast<const T*>(p.z) + int64_t(it) * D, kRowBytes, bar);
   };
   if (tid == kCopyTid) {
     const int n0 = nmine < kStages ? nmine : kStages;
@@ -521,12 +522,6 @@ __global__ void __launch_bounds__(dec::kThreads, 1) decode_state_kernel(RecParam
   const int ot = tid - kOutTid0;  // output column (warps 12-15)
   const float scale = float(1.0 / sqrt(double(D)));
   const float nwf = ot >= 0 ? Io<T>::ld(reinterpret_cast<const T*>(p.norm_w) + ot) : 0.f;
-  auto z_of = [&](int m) -> float {  // gate z of the m-th item for this output column
-    if (ot < 0 || m >= nmine || slot_of(m) < 0) return 0.f;
-    const int it = int(blockIdx.x) + m * grid;
-    return Io<T>::ld(reinterpret_cast<const T*>(p.z) + int64_t(it) * D + ot);
-  };
-  float pz = z_of(0);
 
   bool ok = true;
   for (int m = 0; m < nmine; ++m) {
@@ -537,7 +532,6 @@ __global__ void __launch_bounds__(dec::kThreads, 1) decode_state_kernel(RecParam
     if (slot < 0) {  // a bad slot index: record it, leave every pool row alone
       if (tid == 0 && p.err) atomicExch(p.err, 1);
       if (tid == kCopyTid) refill(m, false);
-      pz = z_of(m + 1);
       continue;
     }
 
@@ -548,6 +542,7 @@ __global__ void __launch_bounds__(dec::kThreads, 1) decode_state_kernel(RecParam
     const T* qh = reinterpret_cast<const T*>(in + 4);
     const T* kh = qh + D;
     const T* vh = kh + D;
+    const T* zh = vh + D;
     float s[kRows][4], kr[kRows], qr[kRows];
 #pragma unroll
     for (int r = 0; r < kRows; ++r) {
@@ -597,8 +592,10 @@ __global__ void __launch_bounds__(dec::kThreads, 1) decode_state_kernel(RecParam
       refill(m, true);
     }
 
-    // D (warps 12-15, while warps 0-11 start the next item): output through the gated RMSNorm
+    // D (warps 12-15, while warps 0-11 start the next item): output through the gated RMSNorm; the
+    // stage (z row) and red[1] are not overwritten before every warp has passed the next item's B
     if (ot >= 0) {
+      const float z = Io<T>::ld(zh + ot);
       float o = 0.f;
 #pragma unroll
       for (int i = 0; i < 16; ++i) o += sm.red[1][i][ot];
@@ -610,9 +607,8 @@ __global__ void __launch_bounds__(dec::kThreads, 1) decode_state_kernel(RecParam
 #pragma unroll
       for (int i = 0; i < D / 32; ++i) tot += sm.snorm[i];
       const float rinv = 1.0f / sqrtf(tot / float(D) + p.eps);
-      o = Io<T>::rnd(nwf * Io<T>::rnd(o * rinv)) * silu_f(pz);
+      o = Io<T>::rnd(nwf * Io<T>::rnd(o * rinv)) * silu_f(z);
       Io<T>::st(reinterpret_cast<T*>(p.out) + int64_t(b) * p.o_sb + int64_t(h) * D + ot, o);
-      pz = z_of(m + 1);
     }
   }
   if (tid == kCopyTid) bulk_wait_all();  // every bulk store has finished before the CTA exits
@@ -771,8 +767,8 @@ extern "C" int gdn_decode_layer(const void* mixed_qkv, int64_t mixed_rs, const v
   const size_t need = gdn_decode_layer_workspace_size(n, Hk, Hv, dk, dv, dtype);
   if (!workspace || workspace_bytes < need)
     return fail(GDN_ERR_WORKSPACE, "gdn_decode_layer: workspace %zu bytes < %zu", workspace_bytes, need);
-  if (!aligned(rec_pool, 16) || !aligned(workspace, 16))
-    return fail(GDN_ERR_ARG, "gdn_decode_layer: rec_pool and the workspace must be 16-byte aligned");
+  if (!aligned(rec_pool, 16) || !aligned(workspace, 16) || !aligned(z, 16))
+    return fail(GDN_ERR_ARG, "gdn_decode_layer: rec_pool, z and the workspace must be 16-byte aligned");
   // conv update of the slot's window + gates + l2norm + recurrence (in place on rec_pool[slot_idx])
   // + gated RMSNorm: two kernels for dk = dv = 128, one (ticket-ordered windows) for 64
   RecParams p{};

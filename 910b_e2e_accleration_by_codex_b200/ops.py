@@ -305,6 +305,8 @@ def decode_layer(mixed_qkv, z, a, b, A_log, dt_bias, conv_w, conv_b, conv_pool, 
     mixed = mixed_qkv.reshape(n, Cc)
     if mixed.stride(1) != 1:
         mixed = mixed.contiguous()
+    if not z.is_contiguous() or z.data_ptr() % 16:  # the state kernel bulk-copies [dv] rows of z
+        z = z.clone(memory_format=torch.contiguous_format)
     K = conv_pool.shape[-1]
     if workspace is None:
         workspace = decode_layer_workspace(n, Hk, Hv, dk, dv, mixed.dtype, mixed.device)

@@ -136,6 +136,8 @@ GDN_API int gdn_recurrent(const void* q, int64_t q_sb, int64_t q_st, const void*
  *   -> l2norm(q), l2norm(k) -> single-step recurrence on rec_pool[slot_idx]
  *   (in place) -> gated RMSNorm with gate z [n, Hv, dv] -> out [n, Hv, dv].
  *   a, b: [n, Hv] (dtype); A_log, dt_bias: [Hv] f32; norm_w: [dv] (dtype).
+ *   z is contiguous and 16-byte aligned (its rows are bulk-copied), as are
+ *   rec_pool and the workspace; otherwise GDN_ERR_ARG.
  * dk = dv = 128: two kernels per call, a prep kernel (conv, l2norm, gates)
  * and a persistent state kernel launched as its programmatic dependent; the
  * workspace (gdn_decode_layer_workspace_size() bytes, 16-byte aligned) carries
