@@ -364,8 +364,8 @@ __global__ void __launch_bounds__(RecShape<DK, DV>::NT, 2) recurrent_kernel(RecP
 //                        traffic never passes through their load/store queues.
 //
 // The state kernel is launched as a programmatic dependent of the prep kernel: it starts while
-// the prep kernel runs, loads the first states (which the prep kernel does not touch), and its
-// copy thread waits for the prep kernel's results (griddepcontrol.wait) before loading them.
+// the prep kernel runs, loads its first state (which the prep kernel does not touch), and its copy
+// thread waits for the prep kernel's results (griddepcontrol.wait) before loading them.
 namespace dec {
 constexpr int D = 128;
 constexpr int kStages = 3;
@@ -503,10 +503,19 @@ __global__ void __launch_bounds__(dec::kThreads, 1) decode_state_kernel(RecParam
     bulk_load(dst + 16 + 3 * kRowBytes, reinterpret_cast<const T*>(p.z) + int64_t(it) * D, kRowBytes, bar);
   };
   if (tid == kCopyTid) {
+    // item 0 first: the states do not depend on the prep kernel, its q/k/v rows and gates do; the
+    // other stages are issued once item 0 has landed, so that it does not share HBM with them
     const int n0 = nmine < kStages ? nmine : kStages;
-    for (int m = 0; m < n0; ++m) load_state(m);      // the states do not depend on the prep kernel
-    asm volatile("griddepcontrol.wait;" ::: "memory");  // its q/k/v rows and gates do
-    for (int m = 0; m < n0; ++m) load_inputs(m);
+    if (n0 > 0) load_state(0);
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    if (n0 > 0) {
+      load_inputs(0);
+      if (slot_of(0) >= 0) mbar_wait(smem_u32(&sm.full[0]), 0u);
+    }
+    for (int m = 1; m < n0; ++m) {
+      load_state(m);
+      load_inputs(m);
+    }
   }
   // copy thread, at the end of item m: the stage of item m - 1 takes item m + 2 once the bulk
   // store of item m - 1 has read it (the store of item m, just issued, may still be reading; an

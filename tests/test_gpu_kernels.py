@@ -297,7 +297,7 @@ def test_chunk_matches_token_recurrence_bf16(ops):
 
 
 # ----------------------------------------------------------------------------- fused decode layer
-def _decode_layer_case(ops, n, S, Hk, Hv, slot, steps, seed=7, conv_b=False, dd=128, K=4):
+def _decode_layer_case(ops, n, S, Hk, Hv, slot, steps, seed=7, conv_b=False, dd=128, K=4, hf=False):
     rng = np.random.default_rng(seed)
     Cc = 2 * Hk * dd + Hv * dd
     bf = torch.bfloat16
@@ -320,7 +320,8 @@ def _decode_layer_case(ops, n, S, Hk, Hv, slot, steps, seed=7, conv_b=False, dd=
         b = r16(rng.standard_normal((n, Hv)))
         # oracle: elem conv -> split -> gates -> recurrence -> gated norm
         st = cp[slot]
-        y = O.conv_update_elem(mixed[:, :, None], st, conv_w, bias, "bf16")[:, :, 0]
+        conv = O.conv_update if hf else O.conv_update_elem
+        y = conv(mixed[:, :, None], st, conv_w, bias, "bf16")[:, :, 0]
         cp[slot] = st
         qo, ko, vo = y[:, :Hk * dd].reshape(n, Hk, dd), y[:, Hk * dd:2 * Hk * dd].reshape(n, Hk, dd), \
             y[:, 2 * Hk * dd:].reshape(n, Hv, dd)
@@ -329,7 +330,8 @@ def _decode_layer_case(ops, n, S, Hk, Hv, slot, steps, seed=7, conv_b=False, dd=
         ref = O.gated_rmsnorm(core, z, norm_w, 1e-6, "bf16")
         out = ops.decode_layer(T(mixed, bf), T(z, bf), T(a, bf), T(b, bf), T(A_log), T(dt_bias), T(conv_w, bf),
                                None if bias is None else T(bias, bf), conv_d, rec_d, slot_d, T(norm_w, bf), 1e-6,
-                               Hk, Hv, dd, dd, workspace=ws)
+                               Hk, Hv, dd, dd, conv_mode=ops.GDN_CONV_HF if hf else ops.GDN_CONV_ELEM,
+                               workspace=ws)
         assert np.array_equal(N(conv_d), cp)
         assert bf16_ok(N(out), ref)
         assert np.abs(N(rec_d)[slot] - rp[slot]).max() < 1e-4
@@ -342,6 +344,16 @@ def test_decode_layer_matches_oracle_composition(ops):
     _decode_layer_case(ops, 5, 8, 2, 6, np.array([6, 1, 3, 0, 4], np.int32), steps=1)
 
 
+def test_decode_layer_hf_conv_mode_with_bias(ops):
+    """HF conv rounding (one rounding of the fp32-accumulated conv plus bias) through the decode layer."""
+    _decode_layer_case(ops, 4, 9, 2, 6, np.array([8, 2, 5, 0], np.int32), steps=2, seed=17, conv_b=True, hf=True)
+
+
+def test_decode_layer_conv_width_3(ops):
+    """Conv kernel width 3 (the window update for K != 4)."""
+    _decode_layer_case(ops, 3, 5, 1, 3, np.array([4, 0, 2], np.int32), steps=2, seed=19, K=3)
+
+
 def test_decode_layer_many_items_per_cta_two_steps(ops):
     # 32 x 16 = 512 (slot, head) items: every CTA of the persistent kernel runs several of them,
     # so each shared-memory stage is reused; two steps check the state and windows carry over
@@ -351,11 +363,11 @@ def test_decode_layer_many_items_per_cta_two_steps(ops):
 
 
 def test_decode_layer_large_batch(ops):
-    # 20 x 48 = 960 (slot, head) items: 7 per persistent CTA, so every stage of the state ring is
-    # reused at least twice
+    # 32 x 48 = 1536 (slot, head) items: 10-11 per persistent CTA, so every stage of the state ring
+    # is reused three times
     rng = np.random.default_rng(9)
-    slot = rng.permutation(24)[:20].astype(np.int32)
-    _decode_layer_case(ops, 20, 24, 16, 48, slot, steps=1, seed=13)
+    slot = rng.permutation(40)[:32].astype(np.int32)
+    _decode_layer_case(ops, 32, 40, 16, 48, slot, steps=1, seed=13)
 
 
 def test_decode_layer_bad_slot_sets_error_flag(ops):
