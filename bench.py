@@ -205,14 +205,17 @@ def allreduce_sum(x: float, world: int) -> float:
 def cpu_prefill_sample(w, seconds: float):
     """The reference's prefill path on the host cores: the torch restatement (oracle/gdn_torch_cpu.py)
     of fast_chunk_gated_delta_rule_v2 (src/gdn_chunk_fast2.py:11-62) in the reference's dtypes, one
-    sequence per call as TPEngine.prefill does, over the workload's sequences in order until
-    ~`seconds` elapse."""
+    sequence per call as TPEngine.prefill does, over the workload's sequences in order (repeated
+    passes) until ~`seconds` elapse."""
     from oracle import gdn_torch_cpu as TC
     r = HV // HK
+    nseq = len(w["lens"])
     toks, used, el = 0, 0, 0.0
     t0 = time.perf_counter()
     with torch.inference_mode():
-        for b, L in enumerate(w["lens"]):
+        while used == 0 or el < seconds:
+            b = used % nseq
+            L = int(w["lens"][b])
             s, e = int(w["cu"][b]), int(w["cu"][b + 1])
             q = w["q"][s:e].repeat_interleave(r, dim=1)[None]
             k = w["k"][s:e].repeat_interleave(r, dim=1)[None]
@@ -221,10 +224,8 @@ def cpu_prefill_sample(w, seconds: float):
             toks += L
             used += 1
             el = time.perf_counter() - t0
-            if el >= seconds:
-                break
-    return toks / el, (f"{used} of {len(w['lens'])} sequences ({toks} tokens), one call per sequence of the torch "
-                       f"restatement of src/gdn_chunk_fast2.py"), el
+    return toks / el, (f"{used} sequence calls ({used / nseq:.1f} passes over the {nseq} sequences, {toks} tokens), "
+                       f"one call per sequence of the torch restatement of src/gdn_chunk_fast2.py"), el
 
 
 def cpu_decode_sample(seconds: float):

@@ -67,6 +67,12 @@ def test_validation_errors_without_gpu(lib):
     # dk = 128: prepared q/k/v rows [n, C] bf16 + gates [n, Hv, 4] f32; dk = 64: a ticket per (slot, k-head)
     assert lib.gdn_decode_layer_workspace_size(16, 16, 48, 128, 128, 1) == 16 * 10240 * 2 + 16 * 48 * 16
     assert lib.gdn_decode_layer_workspace_size(16, 4, 8, 64, 64, 1) >= 16 * 4 * 4
+    # the d = 128 decode layer bulk-copies rows of z: a z that is not 16-byte aligned is refused before
+    # any CUDA call (the other pointers are never dereferenced on this path)
+    ok, odd = 4096, 4096 + 2
+    rc = lib.gdn_decode_layer(ok, 10240, odd, ok, ok, ok, ok, ok, None, ok, ok, ok, 4, ok, 1e-6, ok, 2, 16, 48,
+                              128, 128, 4, L.GDN_CONV_ELEM, ok, 1 << 30, L.GDN_BF16, None, None)
+    assert rc == 1 and b"aligned" in lib.gdn_last_error()
 
 
 def test_ops_refuse_cpu_tensors():
