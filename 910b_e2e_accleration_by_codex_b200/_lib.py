@@ -39,7 +39,15 @@ SIGNATURES = {
     "gdn_chunk_prefill": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _vp, _vp, _i64, _vp, _i32, _i64, _vp, _vp,
                                  _vp, _vp, _vp, _i64, _vp, _i64, _i32, _i32, _i32, _i32, _i32, _i32, _vp,
                                  _vp]),
+    "gdn_ar_buffer_bytes": (_sz, [_i32, _sz, _i32]),
+    "gdn_ar_alloc": (_i32, [_sz, C.POINTER(_vp)]),
+    "gdn_ar_free": (_i32, [_vp]),
+    "gdn_ar_ipc_handle": (_i32, [_vp, _vp]),
+    "gdn_ar_ipc_open": (_i32, [_vp, C.POINTER(_vp)]),
+    "gdn_ar_ipc_close": (_i32, [_vp]),
+    "gdn_allreduce": (_i32, [_vp, _vp, _sz, _i32, _i32, _i32, _vp, _sz, C.c_uint32, _vp, _vp]),
 }
+GDN_IPC_HANDLE_BYTES = 64
 
 _lock = threading.Lock()
 _lib = None

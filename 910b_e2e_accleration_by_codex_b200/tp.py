@@ -7,6 +7,8 @@ Mirrors the reference's src/cb_tp.py:
     k heads (with their q/k conv channels) and v heads (with their v conv channels, a/b/A_log/
     dt_bias rows, z rows and out_proj columns), and a block of MLP columns.
   * ``TPEngine`` (src/cb_tp.py:117-285): the engine on sharded weights.
+  * ``PeerAllReduce``: the sum over ranks for decode-sized outputs by this library's own kernel over
+    IPC-mapped peer buffers (gdn_allreduce); NCCL keeps the larger (prefill) ones.
 One difference: the reference requires the KV-head count to divide the TP degree
 (src/cb_tp.py:54), so 4 KV heads cannot run at TP=8.  Here, when tp > kv heads (tp a multiple of
 them), each KV head is replicated on tp / kvh consecutive ranks, and each rank keeps the q heads
@@ -14,6 +16,7 @@ that read it, so attention is still exact.
 """
 from __future__ import annotations
 
+import ctypes as C
 import datetime
 import os
 
@@ -21,11 +24,103 @@ import torch
 import torch.distributed as dist
 import torch.nn as nn
 
+from . import _lib
 from .engine import CBEngine
 
 
+class PeerAllReduce:
+    """In-place sum over the ranks of the process group (one process per GPU, one node) by
+    gdn_allreduce over IPC-mapped peer buffers, for bf16 outputs of up to ``max_elems`` elements.
+    Collective: every rank constructs it, calls it on tensors of the same sizes in the same order
+    (CUDA-graph capture included) and closes it.  Each rank's result is the fp32 sum in rank order
+    rounded once to bf16, identical on all ranks.  If a rank does not arrive within ``spin_limit``
+    polls the others set ``err`` to 3 and leave their tensor as it was; the instance is then out of
+    step and must be closed."""
+
+    def __init__(self, max_elems, device, spin_limit=0):
+        lib = _lib.load()
+        self.lib = lib
+        self.rank, self.world = dist.get_rank(), dist.get_world_size()
+        self.max_elems = int(max_elems)
+        self.spin_limit = int(spin_limit)
+        nbytes = lib.gdn_ar_buffer_bytes(self.world, self.max_elems, _lib.GDN_BF16)
+        if nbytes == 0:
+            raise RuntimeError(f"PeerAllReduce: world {self.world} not supported (1..8 ranks)")
+        own = C.c_void_p()
+        _lib.check(lib.gdn_ar_alloc(nbytes, C.byref(own)), "gdn_ar_alloc")
+        handle = C.create_string_buffer(_lib.GDN_IPC_HANDLE_BYTES)
+        _lib.check(lib.gdn_ar_ipc_handle(own, handle), "gdn_ar_ipc_handle")
+        handles = [None] * self.world
+        dist.all_gather_object(handles, handle.raw)
+        ptrs = []
+        for r, hb in enumerate(handles):
+            if r == self.rank:
+                ptrs.append(own.value)
+                continue
+            peer = C.c_void_p()
+            _lib.check(lib.gdn_ar_ipc_open(C.create_string_buffer(hb, _lib.GDN_IPC_HANDLE_BYTES), C.byref(peer)),
+                       "gdn_ar_ipc_open")
+            ptrs.append(peer.value)
+        self._own, self._ptrs = own.value, ptrs
+        self._table = (C.c_void_p * self.world)(*ptrs)
+        self.err = torch.zeros(1, dtype=torch.int32, device=device)
+        self.closed = False
+
+    def applies(self, y):
+        """Whether ``y`` goes through this kernel (the same answer on every rank for the same shape)."""
+        return (not self.closed and y.dtype == torch.bfloat16 and y.numel() <= self.max_elems
+                and y.numel() % 8 == 0)
+
+    def __call__(self, y):
+        """Sum ``y`` over the ranks in place; returns ``y``."""
+        if not y.is_contiguous() or y.data_ptr() % 16:
+            z = y.contiguous().clone()
+            self(z)
+            y.copy_(z)
+            return y
+        _lib.check(self.lib.gdn_allreduce(y.data_ptr(), y.data_ptr(), y.numel(), _lib.GDN_BF16, self.rank,
+                                          self.world, self._table, self.max_elems, self.spin_limit,
+                                          self.err.data_ptr(), torch.cuda.current_stream().cuda_stream),
+                   "gdn_allreduce")
+        return y
+
+    def close(self):
+        """Collective: after every rank's last call, unmap the peers' buffers and free this one."""
+        if self.closed:
+            return
+        self.closed = True
+        torch.cuda.synchronize()
+        dist.barrier()
+        for r, ptr in enumerate(self._ptrs):
+            if r != self.rank:
+                _lib.check(self.lib.gdn_ar_ipc_close(ptr), "gdn_ar_ipc_close")
+        dist.barrier()  # no rank writes into this buffer any more
+        _lib.check(self.lib.gdn_ar_free(self._own), "gdn_ar_free")
+
+
+_PEER_AR = None
+
+
+def enable_peer_allreduce(max_elems, device, spin_limit=0):
+    """Collective: route AllReduceLinear's sums of up to ``max_elems`` bf16 elements through a
+    PeerAllReduce (returned); larger ones stay on NCCL."""
+    global _PEER_AR
+    disable_peer_allreduce()
+    _PEER_AR = PeerAllReduce(max_elems, device, spin_limit)
+    return _PEER_AR
+
+
+def disable_peer_allreduce():
+    """Collective: close the PeerAllReduce in use, if any."""
+    global _PEER_AR
+    if _PEER_AR is not None:
+        _PEER_AR.close()
+        _PEER_AR = None
+
+
 class AllReduceLinear(nn.Module):
-    """Row-parallel linear: local partial product, then the sum over ranks (identical on all)."""
+    """Row-parallel linear: local partial product, then the sum over ranks (identical on all):
+    the peer-memory kernel for decode-sized outputs when enabled, NCCL otherwise."""
 
     def __init__(self, lin):
         super().__init__()
@@ -33,7 +128,11 @@ class AllReduceLinear(nn.Module):
 
     def forward(self, x):
         y = self.lin(x)
-        dist.all_reduce(y)
+        ar = _PEER_AR
+        if ar is not None and ar.applies(y):
+            ar(y)
+        else:
+            dist.all_reduce(y)
         return y
 
 
@@ -145,8 +244,31 @@ def init_tp(rank, world, backend="nccl", master_port="29561", timeout_s=120):
 
 
 class TPEngine(CBEngine):
-    """CBEngine on sharded weights (src/cb_tp.py:117-285).  Decode graphs capture the NCCL
-    all-reduces of AllReduceLinear; every rank captures the same sequence of graphs."""
+    """CBEngine on sharded weights (src/cb_tp.py:117-285).  With ``peer_allreduce`` (default) the
+    decode steps' row-parallel sums ([slots, hidden] bf16) go through PeerAllReduce and prefill's
+    larger ones through NCCL; decode graphs capture whichever runs, and every rank captures the same
+    sequence of graphs.  ``close()`` (collective) releases the graphs and the peer buffers."""
 
-    def __init__(self, model, n_slots, t_max, device, tp, graph_decode=False):
+    def __init__(self, model, n_slots, t_max, device, tp, graph_decode=False, peer_allreduce=True):
+        self.peer_ar = None
+        if peer_allreduce and tp > 1:
+            hidden = model.config.text_config.hidden_size
+            self.peer_ar = enable_peer_allreduce(n_slots * hidden, device)
         super().__init__(model, n_slots, t_max, device, graph_decode=graph_decode, tp=tp)
+
+    def check_errors(self):
+        """Raise if a peer all-reduce timed out (a rank did not arrive)."""
+        if self.peer_ar is not None and int(self.peer_ar.err.item()) != 0:
+            raise RuntimeError(f"peer all-reduce error {int(self.peer_ar.err.item())} (a rank did not arrive)")
+
+    def close(self):
+        """Collective: release the decode graphs and the peer all-reduce buffers."""
+        self._graphs.clear()
+        self._graph_out.clear()
+        if self.peer_ar is not None:
+            torch.cuda.synchronize()
+            if _PEER_AR is self.peer_ar:
+                disable_peer_allreduce()
+            else:
+                self.peer_ar.close()
+            self.peer_ar = None

@@ -79,6 +79,8 @@ def parse():
                     help="skip the config 3/4 model leg (the ~27B hybrid with random weights through the engine, "
                          "tensor-parallel over all ranks when launched with more than one)")
     ap.add_argument("--model-steps", type=int, default=32, help="timed decode steps of the model leg")
+    ap.add_argument("--model-allreduce", choices=["peer", "nccl"], default="peer",
+                    help="TP decode sums: this library's peer-memory kernel or NCCL")
     return ap.parse_args()
 
 
@@ -441,8 +443,9 @@ def run_model(args, world, rank, local):
     torch.cuda.empty_cache()
     slots = model_slots(world)
     t_max = 1024
-    eng = (tp_mod.TPEngine(model, slots, t_max, dev, world, graph_decode=True) if world > 1 else
-           eng_mod.CBEngine(model, slots, t_max, dev, graph_decode=True))
+    peer = args.model_allreduce == "peer"
+    eng = (tp_mod.TPEngine(model, slots, t_max, dev, world, graph_decode=True, peer_allreduce=peer) if world > 1
+           else eng_mod.CBEngine(model, slots, t_max, dev, graph_decode=True))
     g = torch.Generator(device="cpu").manual_seed(4321)
     lens = torch.randint(MODEL_PLEN[0], MODEL_PLEN[1] + 1, (slots,), generator=g).tolist()
     prompts = [torch.randint(0, MODEL_TEXT_CONFIG["vocab_size"], (1, L), generator=g) for L in lens]
@@ -469,8 +472,12 @@ def run_model(args, world, rank, local):
     e1.record()
     torch.cuda.synchronize()
     dec_ms = allreduce_max(e0.elapsed_time(e1), world) / args.model_steps
-    eng._graphs.clear()                          # graphs holding NCCL calls go before the process group
-    eng._graph_out.clear()
+    if world > 1:
+        eng.check_errors()
+        eng.close()                              # graphs and peer buffers go before the process group
+    else:
+        eng._graphs.clear()
+        eng._graph_out.clear()
     del eng, model
     torch.cuda.empty_cache()
     n_pre = sum(lens)
@@ -479,6 +486,8 @@ def run_model(args, world, rank, local):
             "prefill_tokens": n_pre, "prefill_ms": pre_ms, "prefill_tokens_per_s": n_pre / (pre_ms / 1e3),
             "decode_steps": args.model_steps, "decode_ms_per_step": dec_ms,
             "decode_tokens_per_s": slots / (dec_ms / 1e3), "graph": True, "weights": "random-init bf16",
+            "allreduce": ("none" if world <= 1 else
+                          "gdn_allreduce (peer memory) for decode, NCCL for prefill" if peer else "NCCL"),
             "prompts": f"uniform random token ids, lengths U[{MODEL_PLEN[0]},{MODEL_PLEN[1]}]",
             "build_s": build_s}
 

@@ -207,6 +207,33 @@ GDN_API int gdn_chunk_prefill(const void* q, int64_t q_st, const void* k, int64_
                       int Hv, int dk, int dv, int use_qk_l2norm, int dtype, int32_t* err_flag,
                       void* stream);
 
+/* ---------------------------------------------------------------------------
+ * a8. Peer-memory all-reduce (sum, bf16) across the ranks of one node, for the
+ * row-parallel projections of the TP engine: replaces the NCCL all-reduce of
+ * AllReduceLinear.forward (src/cb_tp.py:25-35) for decode-sized outputs.
+ * Each rank allocates one buffer of gdn_ar_buffer_bytes(world, max_elems)
+ * with gdn_ar_alloc, exports its IPC handle (GDN_IPC_HANDLE_BYTES bytes) with
+ * gdn_ar_ipc_handle, opens every other rank's handle with gdn_ar_ipc_open, and
+ * passes all world buffer pointers (its own at index rank) to gdn_allreduce.
+ * Every rank makes the same sequence of gdn_allreduce calls with the same n
+ * (like any collective); x and y may alias; n <= max_elems, n a multiple of 8,
+ * x and y 16-byte aligned.  Each rank's result is the fp32 sum of the ranks'
+ * inputs in rank order, rounded once to bf16 (identical on every rank).  A
+ * rank that does not arrive within spin_limit polls (0: 2^22) makes the
+ * others set *err_flag = 3 and leave y untouched.  No multicast memory is
+ * used.  Close peer mappings (gdn_ar_ipc_close) and free the buffer
+ * (gdn_ar_free) only after every rank's last call has completed.
+ */
+#define GDN_IPC_HANDLE_BYTES 64
+GDN_API size_t gdn_ar_buffer_bytes(int world, size_t max_elems, int dtype);
+GDN_API int gdn_ar_alloc(size_t bytes, void** ptr);
+GDN_API int gdn_ar_free(void* ptr);
+GDN_API int gdn_ar_ipc_handle(void* ptr, void* handle);
+GDN_API int gdn_ar_ipc_open(const void* handle, void** ptr);
+GDN_API int gdn_ar_ipc_close(void* ptr);
+GDN_API int gdn_allreduce(const void* x, void* y, size_t n, int dtype, int rank, int world, void* const* bufs,
+                          size_t max_elems, uint32_t spin_limit, int32_t* err_flag, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -63,8 +63,12 @@ def run(engine_cls, model, device, graph, **kw):
     outs = [eng.decode_step([0, 1], t) for t in toks]
     if h is not None:
         h.remove()
-    eng._graphs.clear()
-    eng._graph_out.clear()
+    if hasattr(eng, "close"):
+        eng.check_errors()
+        eng.close()
+    else:
+        eng._graphs.clear()
+        eng._graph_out.clear()
     return outs if graph else logits
 
 
