@@ -220,7 +220,9 @@ GDN_API int gdn_chunk_prefill(const void* q, int64_t q_st, const void* k, int64_
  * x and y 16-byte aligned.  Each rank's result is the fp32 sum of the ranks'
  * inputs in rank order, rounded once to bf16 (identical on every rank).  A
  * rank that does not arrive within spin_limit polls (0: 2^22) makes the
- * others set *err_flag = 3 and leave y untouched.  No multicast memory is
+ * others set *err_flag = 3 and leave y untouched; later calls with the same
+ * err_flag set stop waiting as soon as they would wait (the ranks are out of
+ * step; recreate the buffers).  No multicast memory is
  * used.  Close peer mappings (gdn_ar_ipc_close) and free the buffer
  * (gdn_ar_free) only after every rank's last call has completed.
  */

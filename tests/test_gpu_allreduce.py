@@ -4,9 +4,9 @@ Every rank can regenerate every rank's seeded input, so each checks its result b
 the fp32 sum in rank order rounded once to bf16: over sizes that change from call to call (the
 double-buffered slots alternate), inside a CUDA graph replayed with fresh inputs, and against
 NCCL's sum within bf16 rounding.  A second instance with a short spin limit checks the failure
-path: only rank 0 calls, its wait runs out, it reports error 3 and leaves its tensor untouched,
-and the other rank stays in a host barrier (its buffer mapped, no kernel in flight) until rank 0
-is done.  Skipped when fewer than two GPUs are visible.
+path: only rank 0 calls, its wait runs out, it reports error 3 and leaves its tensor untouched (a
+later call returns without waiting), and the other rank stays in a host barrier (its buffer
+mapped, no kernel in flight) until rank 0 is done.  Skipped when fewer than two GPUs are visible.
 """
 import os
 import socket
@@ -92,6 +92,9 @@ def _rank(rank, world, port, q):
             torch.cuda.synchronize()
             out["timeout_err"] = int(ar2.err.item())
             out["timeout_untouched"] = torch.equal(y.cpu(), inp(0, 7, 5120))
+            ar2(y)                           # out of step now: returns without waiting again
+            torch.cuda.synchronize()
+            out["timeout_untouched"] &= torch.equal(y.cpu(), inp(0, 7, 5120)) and int(ar2.err.item()) == 3
         dist.barrier()                       # rank 1 waits here while rank 0's kernel runs
         ar2.close()
         q.put((rank, out))
