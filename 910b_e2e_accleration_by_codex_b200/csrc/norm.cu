@@ -83,7 +83,80 @@ static int launch_norm(const void* x, int64_t x_rs, const void* gate, int64_t g_
   return check_launch("gdn_gated_rmsnorm");
 }
 
+// Layer RMSNorm, Qwen3_5RMSNorm.forward (transformers modeling_qwen3_5.py): y = rnd(x * rsqrt(mean(x^2)
+// + eps) * (1 + w)) with fp32 statistics and products and one final rounding -- the norm the reference
+// replaces with npu_rms_norm (src/cb_engine.py:62-63, 70-71).  One CTA of 128 threads per row
+// (dim <= 8192); thread t holds the 16-byte groups t, t + 128, ... of the row in registers.
+template <typename T, bool VEC>
+__global__ void __launch_bounds__(128) rmsnorm_kernel(const T* __restrict__ x, int64_t x_rs, const T* __restrict__ w,
+                                                      T* __restrict__ y, int64_t y_rs, int dim, float eps) {
+  constexpr int VW = 16 / int(sizeof(T));  // elements per group
+  constexpr int NV = 8192 / (128 * VW);    // groups per thread at the largest dim
+  __shared__ float red[4];
+  const int tid = threadIdx.x;
+  const T* xr = x + int64_t(blockIdx.x) * x_rs;
+  T* yr = y + int64_t(blockIdx.x) * y_rs;
+  float xv[NV][VW];
+  float ss = 0.f;
+#pragma unroll
+  for (int v = 0; v < NV; ++v) {
+    const int c = (v * 128 + tid) * VW;
+    if (c < dim) {
+      if (VEC) {
+        const uint4 u = *reinterpret_cast<const uint4*>(xr + c);
+        const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+        for (int j = 0; j < VW; ++j) xv[v][j] = Io<T>::ld(e + j);
+      } else {
+#pragma unroll
+        for (int j = 0; j < VW; ++j) xv[v][j] = c + j < dim ? Io<T>::ld(xr + c + j) : 0.f;
+      }
+#pragma unroll
+      for (int j = 0; j < VW; ++j) ss += xv[v][j] * xv[v][j];
+    }
+  }
+  ss = warp_sum(ss);
+  if ((tid & 31) == 0) red[tid >> 5] = ss;
+  __syncthreads();
+  const float r = 1.0f / sqrtf((red[0] + red[1] + red[2] + red[3]) / float(dim) + eps);
+#pragma unroll
+  for (int v = 0; v < NV; ++v) {
+    const int c = (v * 128 + tid) * VW;
+    if (c < dim) {
+#pragma unroll
+      for (int j = 0; j < VW; ++j)
+        if (VEC || c + j < dim) Io<T>::st(yr + c + j, (xv[v][j] * r) * (1.0f + Io<T>::ld(w + c + j)));
+    }
+  }
+}
+
+template <typename T>
+static int launch_rmsnorm(const void* x, int64_t x_rs, const void* w, void* y, int64_t y_rs, int64_t rows, int dim,
+                          float eps, cudaStream_t s) {
+  constexpr int VW = 16 / int(sizeof(T));
+  const bool vec = aligned(x, 16) && aligned(y, 16) && dim % VW == 0 && x_rs % VW == 0 && y_rs % VW == 0;
+  if (vec)
+    rmsnorm_kernel<T, true><<<dim3(unsigned(rows)), 128, 0, s>>>((const T*)x, x_rs, (const T*)w, (T*)y, y_rs, dim, eps);
+  else
+    rmsnorm_kernel<T, false><<<dim3(unsigned(rows)), 128, 0, s>>>((const T*)x, x_rs, (const T*)w, (T*)y, y_rs, dim, eps);
+  return check_launch("gdn_rmsnorm");
+}
+
 }  // namespace gdn
+
+extern "C" int gdn_rmsnorm(const void* x, int64_t x_rs, const void* weight, void* y, int64_t y_rs, int64_t rows,
+                           int dim, float eps, int dtype, void* stream) {
+  using namespace gdn;
+  if (rows < 0 || dim <= 0) return fail(GDN_ERR_ARG, "gdn_rmsnorm: rows=%lld dim=%d", (long long)rows, dim);
+  if (rows == 0) return GDN_OK;
+  if (!x || !weight || !y) return fail(GDN_ERR_ARG, "gdn_rmsnorm: null pointer");
+  if (dim > 8192) return fail(GDN_ERR_SHAPE, "gdn_rmsnorm: dim=%d (<= 8192)", dim);
+  if (rows > 0x7fffffffLL) return fail(GDN_ERR_ARG, "gdn_rmsnorm: rows too large");
+  cudaStream_t s = as_stream(stream);
+  if (dtype == GDN_BF16) return launch_rmsnorm<__nv_bfloat16>(x, x_rs, weight, y, y_rs, rows, dim, eps, s);
+  if (dtype == GDN_F32) return launch_rmsnorm<float>(x, x_rs, weight, y, y_rs, rows, dim, eps, s);
+  return fail(GDN_ERR_DTYPE, "gdn_rmsnorm: dtype %d", dtype);
+}
 
 extern "C" int gdn_gated_rmsnorm(const void* x, int64_t x_rs, const void* gate, int64_t g_rs,
                                  const void* weight, void* y, int64_t y_rs, int64_t rows, int dim,

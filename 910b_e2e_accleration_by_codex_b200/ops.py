@@ -87,6 +87,29 @@ def gated_rmsnorm(x: torch.Tensor, gate: torch.Tensor, weight: torch.Tensor, eps
     return y.view(x.shape)
 
 
+def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Qwen3_5RMSNorm.forward (transformers modeling_qwen3_5.py): x * rsqrt(mean(x^2) + eps) * (1 + weight)
+    in fp32, rounded once to x's dtype -- the layer norm the reference replaces with npu_rms_norm
+    (src/cb_engine.py:62-63)."""
+    _need_cuda(x, weight)
+    dim = x.shape[-1]
+    x2 = x.reshape(-1, dim)
+    if x2.stride(-1) != 1:
+        x2 = x2.contiguous()
+    w = weight.to(x.dtype).contiguous()
+    y = torch.empty(x2.shape, dtype=x.dtype, device=x.device) if out is None else out.view(-1, dim)
+    lib = _lib.load()
+    _lib.check(lib.gdn_rmsnorm(_p(x2), x2.stride(0), _p(w), _p(y), y.stride(0), x2.shape[0], dim, float(eps),
+                               _dtype_code(x), _stream()), "gdn_rmsnorm")
+    return y.view(x.shape)
+
+
+def rmsnorm_forward(self, x):
+    """Bound in place of Qwen3_5RMSNorm.forward, where the reference binds npu_rms_norm
+    (src/cb_engine.py:62-63, 70-71)."""
+    return rmsnorm(x, self.weight, self.eps)
+
+
 def rmsnorm_gated_forward(self, hidden_states, gate=None):
     """Bound in place of Qwen3_5RMSNormGated.forward (src/cb_engine.py:65-67, 72-73)."""
     return gated_rmsnorm(hidden_states, gate, self.weight, self.variance_epsilon)

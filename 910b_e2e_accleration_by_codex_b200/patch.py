@@ -1,9 +1,9 @@
 """patch_model: install the CUDA GDN operators on HF Qwen3.5 modules.
 
 Mirrors the reference's ``patch_model(model, fast_gdn, gdn_v2)`` (src/cb_engine.py:54-77): the
-same attributes of ``Qwen3_5GatedDeltaNet`` and the forward of ``Qwen3_5RMSNormGated`` are
-rebound, so HF's own forward (and any engine that calls those attributes) runs the B200 kernels.
-The layer RMSNorm (``Qwen3_5RMSNorm``) keeps HF's forward: it is not part of the GDN path.
+same attributes of ``Qwen3_5GatedDeltaNet`` and the forwards of ``Qwen3_5RMSNormGated`` and of
+the layer norm ``Qwen3_5RMSNorm`` are rebound, so HF's own forward (and any engine that calls
+those attributes) runs the B200 kernels.
 """
 from __future__ import annotations
 
@@ -25,7 +25,9 @@ def patch_model(model, fast_gdn: bool = True, gdn_v2: bool = True):
 
     n_gdn = 0
     for m in model.modules():
-        if isinstance(m, M.Qwen3_5RMSNormGated):
+        if isinstance(m, M.Qwen3_5RMSNorm):
+            m.forward = types.MethodType(ops.rmsnorm_forward, m)
+        elif isinstance(m, M.Qwen3_5RMSNormGated):
             m.forward = types.MethodType(ops.rmsnorm_gated_forward, m)
         elif isinstance(m, M.Qwen3_5GatedDeltaNet):
             m.recurrent_gated_delta_rule = ops.recurrent_gated_delta_rule

@@ -440,6 +440,9 @@ def run_model(args, world, rank, local):
     params = sum(p.numel() for n, p in model.named_parameters() if "visual" not in n)
     if world > 1:
         tp_mod.shard_model(model, rank, world)
+    # as the reference's runs do before building the engine (src/cb_run.py:158): the layer RMSNorms
+    # and the GDN plug-in points of the HF modules go to this library's kernels
+    importlib.import_module(f"{PKG}.patch").patch_model(model, fast_gdn=True, gdn_v2=True)
     torch.cuda.empty_cache()
     slots = model_slots(world)
     t_max = 1024

@@ -208,6 +208,16 @@ GDN_API int gdn_chunk_prefill(const void* q, int64_t q_st, const void* k, int64_
                       void* stream);
 
 /* ---------------------------------------------------------------------------
+ * Layer RMSNorm of the hybrid model, Qwen3_5RMSNorm.forward (transformers
+ * modeling_qwen3_5.py): y = x * rsqrt(mean(x^2) + eps) * (1 + weight) in fp32,
+ * rounded once to dtype; the norm the reference replaces with npu_rms_norm in
+ * patch_model (src/cb_engine.py:62-63, 70-71).  x, y: [rows, dim] with row
+ * strides x_rs, y_rs (elements); weight [dim] in dtype; dim <= 8192.
+ */
+GDN_API int gdn_rmsnorm(const void* x, int64_t x_rs, const void* weight, void* y, int64_t y_rs, int64_t rows,
+                        int dim, float eps, int dtype, void* stream);
+
+/* ---------------------------------------------------------------------------
  * a8. Peer-memory all-reduce (sum, bf16) across the ranks of one node, for the
  * row-parallel projections of the TP engine: replaces the NCCL all-reduce of
  * AllReduceLinear.forward (src/cb_tp.py:25-35) for decode-sized outputs.

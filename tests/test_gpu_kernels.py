@@ -297,6 +297,30 @@ def test_chunk_matches_token_recurrence_bf16(ops):
 
 
 # ----------------------------------------------------------------------------- fused decode layer
+def test_rmsnorm_matches_hf_module(ops):
+    """ops.rmsnorm == Qwen3_5RMSNorm.forward (fp32 statistics, x * r * (1 + w), one rounding) within one
+    bf16 step (the row reduction order differs from torch's); fp32 rows within 1e-5 relative."""
+    from transformers.models.qwen3_5.modeling_qwen3_5 import Qwen3_5RMSNorm
+    torch.manual_seed(3)
+    for dim, rows, dt in ((5120, 16, torch.bfloat16), (256, 384, torch.bfloat16), (1000, 7, torch.bfloat16),
+                          (5120, 3, torch.float32), (8192, 2, torch.bfloat16)):
+        m = Qwen3_5RMSNorm(dim, eps=1e-6).to(DEV)
+        with torch.no_grad():
+            m.weight.normal_(0, 0.2)
+        m = m.to(dt)
+        x = (torch.randn(rows, dim, device=DEV) * 3).to(dt)
+        ref = m(x).float()
+        got = ops.rmsnorm(x, m.weight, m.eps).float()
+        tol = ref.abs() * (2.0 ** -7 if dt == torch.bfloat16 else 1e-5) + 1e-6
+        assert ((got - ref).abs() <= tol).all(), (dim, rows, dt)
+    # a strided view (q_norm on the chunked q projection): rows of hd inside rows of 2 hd
+    qg = torch.randn(4, 1, 6, 512, device=DEV).to(torch.bfloat16)
+    q, _ = torch.chunk(qg, 2, dim=-1)
+    m = Qwen3_5RMSNorm(256, eps=1e-6).to(DEV).to(torch.bfloat16)
+    assert ((ops.rmsnorm(q, m.weight, m.eps).float() - m(q).float()).abs()
+            <= m(q).float().abs() * 2.0 ** -7 + 1e-6).all()
+
+
 def _decode_layer_case(ops, n, S, Hk, Hv, slot, steps, seed=7, conv_b=False, dd=128, K=4, hf=False):
     rng = np.random.default_rng(seed)
     Cc = 2 * Hk * dd + Hv * dd
