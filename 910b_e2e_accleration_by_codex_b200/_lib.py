@@ -40,6 +40,9 @@ SIGNATURES = {
                                  _vp, _vp, _vp, _i64, _vp, _i64, _i32, _i32, _i32, _i32, _i32, _i32, _vp,
                                  _vp]),
     "gdn_rmsnorm": (_i32, [_vp, _i64, _vp, _vp, _i64, _i64, _i32, _f32, _i32, _vp]),
+    "gdn_attn_decode_workspace_size": (_sz, [_i32, _i32, _i32, _i32]),
+    "gdn_attn_decode": (_i32, [_vp, _vp, _vp, _vp, _vp, _i64, _i32, _vp, _vp, _i32, _vp, _f32, _vp, _i32, _i32,
+                               _i32, _i32, _vp, _sz, _i32, _vp, _vp]),
     "gdn_ar_buffer_bytes": (_sz, [_i32, _sz, _i32]),
     "gdn_ar_alloc": (_i32, [_sz, C.POINTER(_vp)]),
     "gdn_ar_free": (_i32, [_vp]),

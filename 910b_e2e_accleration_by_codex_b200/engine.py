@@ -79,11 +79,14 @@ class CBEngine:
                     eps=float(getattr(gd.norm, "variance_epsilon", getattr(gd.norm, "eps", 1e-6))))
                 ws_bytes = max(ws_bytes, ops.decode_layer_workspace_bytes(n_slots, Hk, Hv, dk, dv, bf))
         self._ws = torch.zeros(max(ws_bytes, 256), dtype=torch.uint8, device=self.dev)  # decode tickets
+        hq_max = max([self.lm.layers[i].self_attn.q_proj.weight.shape[0] // (2 * self.lm.layers[i].self_attn.head_dim)
+                      for i, t in enumerate(cfg.layer_types) if t == "full_attention"] or [1])
+        hd_max = max([self.lm.layers[i].self_attn.head_dim
+                      for i, t in enumerate(cfg.layer_types) if t == "full_attention"] or [8])
+        self._attn_ws = ops.attn_decode_workspace(n_slots, hq_max, hd_max, t_max, self.dev)
         self._tok = torch.zeros(n_slots, dtype=torch.long, device=self.dev)
         self._pos = torch.zeros(n_slots, dtype=torch.long, device=self.dev)
         self._slot = torch.arange(n_slots, dtype=torch.int32, device=self.dev)
-        self._all_idx = torch.arange(n_slots, dtype=torch.long, device=self.dev)
-        self._head_off = {}
         self.graph_decode = graph_decode
         self._graphs, self._graph_out = {}, {}
         if graph_decode:
@@ -124,34 +127,23 @@ class CBEngine:
         self.lens = [0] * self.N
 
     # ------------------------------------------------------------------ decode
-    def _kv_rows(self, pos):
-        # flat row index into kv.view(-1, hd) for (slot i, kv head, position pos[i]), i = 0..N-1
-        kvh = next(iter(self.kv_k.values())).shape[1]
-        if "off" not in self._head_off:
-            self._head_off["off"] = (torch.arange(kvh, device=self.dev) * self.T)[None, :]
-        return (self._all_idx[:, None] * (kvh * self.T) + self._head_off["off"] + pos[:, None]).reshape(-1)
-
-    def _attn(self, at, i, h, cos, sin, pos, Lmax, mask):
+    def _attn(self, at, i, h, cos, sin, pos32, Lmax):
+        """Decode attention (src/cb_engine.py:295-316): projections, q/k norms and rotary as the
+        reference; the K/V row write, the attention over positions 0..pos of each slot and the
+        sigmoid output gate in one library call (gdn_attn_decode) instead of index_copy_ + masked
+        SDPA over the Lmax bucket + gate."""
         n = h.shape[0]
         hd = at.head_dim
         kvh = self.kv_k[i].shape[1]
         qg = at.q_proj(h).view(n, 1, -1, hd * 2)
         q, gate = torch.chunk(qg, 2, dim=-1)
-        gate = gate.reshape(n, 1, -1)
         q = at.q_norm(q).transpose(1, 2)
         k = at.k_norm(at.k_proj(h).view(n, 1, kvh, hd)).transpose(1, 2)
         v = at.v_proj(h).view(n, 1, kvh, hd).transpose(1, 2)
         q, k = self.M.apply_rotary_pos_emb(q, k, cos, sin)
-        rows = self._kv_rows(pos)
-        self.kv_k[i].view(-1, hd).index_copy_(0, rows, k[:, :, 0, :].reshape(-1, hd))
-        self.kv_v[i].view(-1, hd).index_copy_(0, rows, v[:, :, 0, :].reshape(-1, hd))
-        Kg = self.kv_k[i][:n, :, :Lmax]
-        Vg = self.kv_v[i][:n, :, :Lmax]
-        g = q.shape[1] // kvh
-        qk = q.reshape(n, kvh, g, hd)
-        o = F.scaled_dot_product_attention(qk, Kg, Vg, attn_mask=mask.expand(n, 1, g, Lmax), scale=at.scaling)
-        o = o.reshape(n, 1, -1) * torch.sigmoid(gate)
-        return at.o_proj(o)
+        o = ops.attn_decode(q[:, :, 0], k[:, :, 0], v[:, :, 0], self.kv_k[i], self.kv_v[i], self._slot, pos32, Lmax,
+                            at.scaling, gate=gate, workspace=self._attn_ws)
+        return at.o_proj(o.reshape(n, 1, -1))
 
     def _gdn(self, gd, i, h):
         n = h.shape[0]
@@ -168,14 +160,14 @@ class CBEngine:
     def _core(self, Lmax):
         """One decode step for all N slots from the static buffers (capturable)."""
         N, pos = self.N, self._pos
-        mask = (torch.arange(Lmax, device=self.dev)[None, :] <= pos[:, None])[:, None, None, :]
+        pos32 = pos.to(torch.int32)
         x = self.lm.embed_tokens(self._tok[:, None])
         pos3 = pos.view(1, N, 1).expand(3, N, 1)
         cos, sin = self.lm.rotary_emb(x, pos3)
         for i, layer in enumerate(self.lm.layers):
             h = layer.input_layernorm(x)
             if self.cfg.layer_types[i] == "full_attention":
-                h = self._attn(layer.self_attn, i, h, cos, sin, pos, Lmax, mask)
+                h = self._attn(layer.self_attn, i, h, cos, sin, pos32, Lmax)
             else:
                 h = self._gdn(layer.linear_attn, i, h)
             x = x + h

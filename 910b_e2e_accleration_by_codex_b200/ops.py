@@ -104,6 +104,35 @@ def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6, out: torch
     return y.view(x.shape)
 
 
+def attn_decode_workspace(n, Hq, hd, max_len, device):
+    """Workspace for ``attn_decode`` (split partials; no zero-fill needed)."""
+    nb = int(_lib.load().gdn_attn_decode_workspace_size(n, Hq, hd, max_len))
+    return torch.empty(max(nb, 16), dtype=torch.uint8, device=device)
+
+
+def attn_decode(q, k_new, v_new, kv_k, kv_v, slot_idx, pos, max_len, scale, gate=None, out=None, workspace=None,
+                err=None):
+    """Slot-indexed attention decode over the KV pool (CBEngine._attn, src/cb_engine.py:295-316): writes
+    k_new/v_new [n, kvh, hd] at pos[n] of kv_k/kv_v[slot_idx] ([n_slots, kvh, T, hd]) and returns
+    softmax(scale q k^T) v over positions 0..pos for q [n, Hq, hd] (kv-major head groups), times
+    sigmoid(gate) [n, Hq, hd] when given, in bf16."""
+    _need_cuda(q, k_new, v_new, kv_k, kv_v, slot_idx, pos)
+    n, Hq, hd = q.shape[0], q.shape[-2], q.shape[-1]
+    kvh, T = kv_k.shape[1], kv_k.shape[2]
+    q = q.reshape(n, Hq, hd).contiguous()
+    k_new = k_new.reshape(n, kvh, hd).contiguous()
+    v_new = v_new.reshape(n, kvh, hd).contiguous()
+    g = None if gate is None else gate.reshape(n, Hq, hd).contiguous()
+    ws = attn_decode_workspace(n, Hq, hd, max_len, q.device) if workspace is None else workspace
+    o = torch.empty(n, Hq, hd, dtype=q.dtype, device=q.device) if out is None else out
+    lib = _lib.load()
+    _lib.check(lib.gdn_attn_decode(_p(q), _p(k_new), _p(v_new), _p(kv_k), _p(kv_v), kv_k.shape[0], T,
+                                   _p(_i32(slot_idx)), _p(_i32(pos)), int(max_len), _p(g), float(scale), _p(o), n,
+                                   Hq, kvh, hd, _p(ws), ws.numel(), _dtype_code(q), _p(err), _stream()),
+               "gdn_attn_decode")
+    return o
+
+
 def rmsnorm_forward(self, x):
     """Bound in place of Qwen3_5RMSNorm.forward, where the reference binds npu_rms_norm
     (src/cb_engine.py:62-63, 70-71)."""

@@ -218,6 +218,27 @@ GDN_API int gdn_rmsnorm(const void* x, int64_t x_rs, const void* weight, void* y
                         int dim, float eps, int dtype, void* stream);
 
 /* ---------------------------------------------------------------------------
+ * Slot-indexed attention decode of the hybrid model's full-attention layers
+ * over the engine's KV pool, replacing CBEngine._attn's index_copy_ of the new
+ * K/V rows, masked SDPA over a 512-token bucket and sigmoid output gate
+ * (src/cb_engine.py:295-316; bucket logic :174-187).  Entry b writes k_new[b],
+ * v_new[b] ([kvh, hd]) at position pos[b] of pool row slot_idx[b] (pools
+ * [n_slots, kvh, T, hd] bf16) and attends q[b] ([Hq, hd], query head h reads
+ * kv head h / (Hq/kvh)) over positions 0..pos[b] with softmax(scale q.k) in
+ * fp32; the output [n, Hq, hd] is rounded to bf16 and, when gate is not NULL,
+ * multiplied by rnd(sigmoid(gate)) ([n, Hq, hd]) and rounded again.
+ * pos[b] < max_len <= T; Hq/kvh <= 8; hd <= 256, a multiple of 8; workspace of
+ * gdn_attn_decode_workspace_size(n, Hq, hd, max_len) bytes.  A bad slot or
+ * position sets *err_flag = 1 and yields zeros for that entry.
+ */
+GDN_API size_t gdn_attn_decode_workspace_size(int n, int Hq, int hd, int max_len);
+GDN_API int gdn_attn_decode(const void* q, const void* k_new, const void* v_new, void* kv_k, void* kv_v,
+                            int64_t n_slots, int T, const int32_t* slot_idx, const int32_t* pos, int max_len,
+                            const void* gate, float scale, void* out, int n, int Hq, int kvh, int hd,
+                            void* workspace, size_t workspace_bytes, int dtype, int32_t* err_flag,
+                            void* stream);
+
+/* ---------------------------------------------------------------------------
  * a8. Peer-memory all-reduce (sum, bf16) across the ranks of one node, for the
  * row-parallel projections of the TP engine: replaces the NCCL all-reduce of
  * AllReduceLinear.forward (src/cb_tp.py:25-35) for decode-sized outputs.

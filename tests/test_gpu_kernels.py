@@ -321,6 +321,49 @@ def test_rmsnorm_matches_hf_module(ops):
             <= m(q).float().abs() * 2.0 ** -7 + 1e-6).all()
 
 
+def test_attn_decode_matches_sdpa(ops):
+    """gdn_attn_decode == the reference's decode attention (src/cb_engine.py:295-316): the new K/V rows
+    land bit-exactly at (slot, pos) and nowhere else, and the output equals softmax(scale q k^T) v over
+    positions 0..pos (fp32) rounded to bf16 times rnd(sigmoid(gate)), within bf16 rounding.  Positions at
+    the 128-position split boundaries and 0 included; a bad slot sets the error flag."""
+    torch.manual_seed(11)
+    bf = torch.bfloat16
+    n, S_, kvh, g, hd, T = 6, 9, 2, 6, 256, 600
+    Hq = kvh * g
+    kv_k = torch.randn(S_, kvh, T, hd, device=DEV).to(bf)
+    kv_v = torch.randn(S_, kvh, T, hd, device=DEV).to(bf)
+    k0, v0 = kv_k.clone(), kv_v.clone()
+    slot = torch.tensor([3, 0, 8, 5, 1, 6], dtype=torch.int32, device=DEV)
+    pos = torch.tensor([0, 127, 128, 255, 431, 599], dtype=torch.int32, device=DEV)
+    q = torch.randn(n, Hq, hd, device=DEV).to(bf)
+    kn = torch.randn(n, kvh, hd, device=DEV).to(bf)
+    vn = torch.randn(n, kvh, hd, device=DEV).to(bf)
+    gate = torch.randn(n, Hq, hd, device=DEV).to(bf)
+    scale = hd ** -0.5
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    out = ops.attn_decode(q, kn, vn, kv_k, kv_v, slot, pos, T, scale, gate=gate, err=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    for b in range(n):
+        s, p_ = int(slot[b]), int(pos[b])
+        k0[s, :, p_] = kn[b]
+        v0[s, :, p_] = vn[b]
+    assert torch.equal(kv_k, k0) and torch.equal(kv_v, v0)
+    for b in range(n):
+        s, p_ = int(slot[b]), int(pos[b])
+        for h in range(Hq):
+            j = h // g
+            sc = (q[b, h].float() @ k0[s, j, :p_ + 1].float().T) * scale
+            o = (torch.softmax(sc, -1) @ v0[s, j, :p_ + 1].float()).to(bf).float()
+            ref = (o * torch.sigmoid(gate[b, h].float()).to(bf).float()).to(bf).float()
+            got = out[b, h].float()
+            assert ((got - ref).abs() <= ref.abs() * 2 ** -6 + 2e-3).all(), (b, h, (got - ref).abs().max())
+    bad = torch.tensor([2, 9, 0, 1, 4, 7], dtype=torch.int32, device=DEV)  # 9 is out of range
+    ops.attn_decode(q, kn, vn, kv_k, kv_v, bad, pos, T, scale, gate=gate, err=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 1
+
+
 def _decode_layer_case(ops, n, S, Hk, Hv, slot, steps, seed=7, conv_b=False, dd=128, K=4, hf=False):
     rng = np.random.default_rng(seed)
     Cc = 2 * Hk * dd + Hv * dd
