@@ -47,7 +47,7 @@ __device__ __forceinline__ void unpack8(const uint4& u, float* f) {
   }
 }
 
-// Warp w streams the split's positions in groups of kU: group i holds positions
+// Warp w streams the split's positions in groups of kU = 4: group i holds positions
 // t0 + (i * kW + w) * kU + u.  Lane l holds dims [8 l, 8 l + 8) of the G query rows (scaled) and
 // of its running outputs; it loads the group's kU 16-byte K and V chunks at once (a warp reads
 // whole 512-byte rows), reduces the G x kU scores across the warp, and applies one online-softmax
