@@ -73,6 +73,24 @@ def test_validation_errors_without_gpu(lib):
     rc = lib.gdn_decode_layer(ok, 10240, odd, ok, ok, ok, ok, ok, None, ok, ok, ok, 4, ok, 1e-6, ok, 2, 16, 48,
                               128, 128, 4, L.GDN_CONV_ELEM, ok, 1 << 30, L.GDN_BF16, None, None)
     assert rc == 1 and b"aligned" in lib.gdn_last_error()
+    # layer RMSNorm, attention decode and peer all-reduce: argument checks before any CUDA call
+    assert lib.gdn_rmsnorm(ok, 8192, ok, ok, 8192, 4, 9000, 1e-6, L.GDN_BF16, None) == 2
+    assert b"8192" in lib.gdn_last_error()
+    assert lib.gdn_rmsnorm(ok, 64, ok, ok, 64, 0, 64, 1e-6, L.GDN_BF16, None) == 0        # no rows: no-op
+    assert lib.gdn_attn_decode_workspace_size(16, 24, 256, 1024) == 16 * 24 * 8 * 258 * 4
+    rc = lib.gdn_attn_decode(ok, ok, ok, ok, ok, 17, 1024, ok, ok, 1024, None, 0.0625, ok, 16, 24, 5, 256, ok,
+                             1 << 30, L.GDN_BF16, None, None)                          # 24 q heads over 5 kv heads
+    assert rc == 2 and b"Hq" in lib.gdn_last_error()
+    rc = lib.gdn_attn_decode(ok, ok, ok, ok, ok, 17, 1024, ok, ok, 1024, None, 0.0625, ok, 16, 24, 4, 256, ok,
+                             64, L.GDN_BF16, None, None)
+    assert rc == 5 and b"workspace" in lib.gdn_last_error()
+    assert lib.gdn_ar_buffer_bytes(9, 1024, L.GDN_BF16) == 0                           # world 1..8
+    assert lib.gdn_ar_buffer_bytes(2, 1024, L.GDN_BF16) == 16384 + 2 * 2 * 2048
+    table = (ctypes.c_void_p * 2)(ok, ok)
+    rc = lib.gdn_allreduce(ok, ok, 2048, L.GDN_BF16, 0, 2, table, 1024, 0, None, None)  # n > slot
+    assert rc == 1 and b"slot" in lib.gdn_last_error()
+    rc = lib.gdn_allreduce(ok, ok, 16, L.GDN_BF16, 2, 2, table, 1024, 0, None, None)    # rank >= world
+    assert rc == 1 and b"rank" in lib.gdn_last_error()
 
 
 def test_ops_refuse_cpu_tensors():
