@@ -155,8 +155,9 @@ __device__ __forceinline__ void tri_inverse64(float* X, float* P, int warp, int 
     }
   }
   group_sync(1);
-  {  // level 1: merge m = lane / 16 (blocks (0,1) or (2,3)), column c = lane % 16, rows 2w, 2w+1
-    const int m = lane >> 4, c = lane & 15, lo = m * 32, hi = lo + 16, r0 = 2 * warp;
+  {  // level 1: merge m = warp / 4 (blocks (0,1) or (2,3)), column c = lane % 16, rows r0, r0 + 1 with
+     // r0 = 4 (warp % 4) + 2 (lane / 16): the half-warps read the same column (a broadcast)
+    const int m = warp >> 2, c = lane & 15, lo = m * 32, hi = lo + 16, r0 = 4 * (warp & 3) + 2 * (lane >> 4);
     float a[2] = {0.f, 0.f};
 #pragma unroll
     for (int tq = 0; tq < 4; ++tq) {
@@ -517,8 +518,13 @@ __global__ void __launch_bounds__(kNT, 1)
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
               const int s = 32 * half + j;
-              Xs[i * LT + s] = (s < i) ? -(a[j] * f * cv.rn[64 + s]) * ex2(gi - cv.gc[s]) : 0.f;
+              a[j] = (s < i) ? -(a[j] * f * cv.rn[64 + s]) * ex2(gi - cv.gc[s]) : 0.f;
             }
+            // 16-byte stores: lanes are rows LT floats apart, so scalar stores would hit 8 banks
+#pragma unroll
+            for (int q4 = 0; q4 < 8; ++q4)
+              *reinterpret_cast<float4*>(Xs + i * LT + 32 * half + 4 * q4) =
+                  make_float4(a[4 * q4], a[4 * q4 + 1], a[4 * q4 + 2], a[4 * q4 + 3]);
           }
         }
       }
