@@ -39,6 +39,9 @@ SIGNATURES = {
     "gdn_chunk_prefill": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _vp, _vp, _i64, _vp, _i32, _i64, _vp, _vp,
                                  _vp, _vp, _vp, _i64, _vp, _i64, _i32, _i32, _i32, _i32, _i32, _i32, _vp,
                                  _vp]),
+    "gdn_chunk_prefill_gates": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _vp, _vp, _i64, _vp, _vp, _vp, _i32, _i64,
+                                       _vp, _vp, _vp, _vp, _vp, _i64, _vp, _i64, _i32, _i32, _i32, _i32, _i32,
+                                       _i32, _vp, _vp]),
     "gdn_rmsnorm": (_i32, [_vp, _i64, _vp, _vp, _i64, _i64, _i32, _f32, _i32, _vp]),
     "gdn_attn_decode_workspace_size": (_sz, [_i32, _i32, _i32, _i32]),
     "gdn_attn_decode": (_i32, [_vp, _vp, _vp, _vp, _vp, _i64, _i32, _vp, _vp, _i32, _vp, _f32, _vp, _i32, _i32,

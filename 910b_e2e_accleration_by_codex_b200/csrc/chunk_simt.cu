@@ -139,8 +139,10 @@ __global__ void __launch_bounds__(kNT, 1) chunk_simt_kernel(ChunkParams p) {
     }
     if (tid < kC) {
       const bool live = tid < nt;
-      sb[tid] = live ? p.beta[(c0 + tid) * p.gb_st + h] : 0.f;
-      gc[tid] = live ? p.g[(c0 + tid) * p.gb_st + h] : 0.f;
+      float gt = 0.f, bt = 0.f;
+      if (live) chunk_gate(p, c0 + tid, h, gt, bt);
+      sb[tid] = bt;
+      gc[tid] = gt;
     }
     __syncthreads();
     // ---- cumulative log-decay within the chunk (warp 0, two entries per lane)

@@ -415,10 +415,9 @@ __global__ void __launch_bounds__(kNT, 1)
     auto load_gates = [&](const Cur& x) {
       const int64_t c0 = x.it.s0 + int64_t(x.ci) * kC, s1 = x.it.s1;
       const int t0 = 2 * lane, t1 = 2 * lane + 1, h = x.it.h;
-      pg0 = c0 + t0 < s1 ? p.g[(c0 + t0) * p.gb_st + h] : 0.f;
-      pg1 = c0 + t1 < s1 ? p.g[(c0 + t1) * p.gb_st + h] : 0.f;
-      pb0 = c0 + t0 < s1 ? p.beta[(c0 + t0) * p.gb_st + h] : 0.f;
-      pb1 = c0 + t1 < s1 ? p.beta[(c0 + t1) * p.gb_st + h] : 0.f;
+      pg0 = pg1 = pb0 = pb1 = 0.f;
+      if (c0 + t0 < s1) chunk_gate(p, c0 + t0, h, pg0, pb0);
+      if (c0 + t1 < s1) chunk_gate(p, c0 + t1, h, pg1, pb1);
     };
     Cur cur, nx;
     seek(cur, 0);

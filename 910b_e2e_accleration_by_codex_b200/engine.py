@@ -247,9 +247,9 @@ class CBEngine:
         q = y[:, :Hk * dk].view(T, Hk, dk)
         k = y[:, Hk * dk:2 * Hk * dk].view(T, Hk, dk)
         v = y[:, 2 * Hk * dk:].view(T, Hv, dv)
-        beta = b.sigmoid().float()
-        g = -p["A_log"].exp() * F.softplus(a.float() + p["dt_bias"])
-        core = ops.chunk_prefill_varlen(q, k, v, g, beta, cu_d, self.rec[i], slot_t, use_init, True)
+        # beta = sigmoid(b) and g = -exp(A_log) softplus(a + dt_bias) are formed inside the kernel
+        core = ops.chunk_prefill_varlen_gates(q, k, v, a, b, p["A_log"], p["dt_bias"], cu_d, self.rec[i], slot_t,
+                                              use_init, True)
         core = ops.gated_rmsnorm(core, z, p["norm_w"], p["eps"])
         return gd.out_proj(core.reshape(1, T, -1))
 

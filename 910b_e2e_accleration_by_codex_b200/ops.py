@@ -306,6 +306,41 @@ def chunk_prefill_varlen(q, k, v, g, beta, cu_seqlens, state_pool=None, slot_idx
     return o
 
 
+def chunk_prefill_varlen_gates(q, k, v, a, b, A_log, dt_bias, cu_seqlens, state_pool=None, slot_idx=None,
+                               use_initial=None, use_qk_l2norm=True, out=None, err=None):
+    """``chunk_prefill_varlen`` with the prefill's gate lines (src/cb_tp.py:170-171, transformers
+    :491-493) done inside the kernel: a, b are the in_proj_a / in_proj_b outputs [T,Hv] in the
+    activations' dtype, A_log / dt_bias [Hv]; beta = sigmoid(b) in that dtype and
+    g = -exp(A_log) * softplus(float(a) + dt_bias) in fp32, bit-identical to those torch lines."""
+    _need_cuda(q, k, v, a, b, A_log, dt_bias, cu_seqlens, state_pool)
+    T, Hk, dk = q.shape
+    Hv, dv = v.shape[1], v.shape[2]
+    for t, d in ((q, dk), (k, dk), (v, dv)):
+        if t.stride(-1) != 1 or t.stride(-2) != d:
+            raise ValueError("q/k/v must have packed heads and unit stride in the last dim")
+    if a.shape != (T, Hv) or b.shape != (T, Hv):
+        raise ValueError(f"a/b must be [T, Hv] = [{T}, {Hv}], got {tuple(a.shape)} / {tuple(b.shape)}")
+    a = a.to(q.dtype)
+    b = b.to(q.dtype)
+    if a.stride(-1) != 1 or b.stride(-1) != 1 or a.stride(0) != b.stride(0):
+        a, b = a.contiguous(), b.contiguous()
+    A_log = A_log.to(torch.float32).contiguous()
+    dt_bias = dt_bias.to(torch.float32).contiguous()
+    o = torch.empty(T, Hv, dv, dtype=q.dtype, device=q.device) if out is None else out
+    B = cu_seqlens.numel() - 1
+    si = _i32(slot_idx)
+    ui = _i32(use_initial)
+    init_pool = None if use_initial is None else state_pool
+    lib = _lib.load()
+    _lib.check(lib.gdn_chunk_prefill_gates(_p(q), q.stride(0), _p(k), k.stride(0), _p(v), v.stride(0), _p(a), _p(b),
+                                           a.stride(0), _p(A_log), _p(dt_bias), _p(_i32(cu_seqlens)), B, T,
+                                           _p(init_pool), _p(si), _p(ui), _p(state_pool), _p(si),
+                                           0 if state_pool is None else state_pool.shape[0], _p(o), o.stride(0),
+                                           Hk, Hv, dk, dv, int(bool(use_qk_l2norm)), _dtype_code(q), _p(err),
+                                           _stream()), "gdn_chunk_prefill_gates")
+    return o
+
+
 # ============================================================================ prefill conv
 def prefill_conv_varlen(x, cu_seqlens, weight, bias=None, conv_pool=None, slot_idx=None, use_initial=None,
                         out=None, err=None):

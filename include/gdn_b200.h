@@ -208,6 +208,26 @@ GDN_API int gdn_chunk_prefill(const void* q, int64_t q_st, const void* k, int64_
                       void* stream);
 
 /* ---------------------------------------------------------------------------
+ * a1 with the gate formation of the GDN prefill fused into the kernel.
+ * Replaces the gate lines of TPEngine.prefill / prefill_chunk
+ * (src/cb_tp.py:170-171, :250-251) and of Qwen3_5GatedDeltaNet.forward
+ * (transformers :491-493) together with the
+ * chunk rule they feed:
+ *   beta = sigmoid(b) rounded to dtype, g = -exp(A_log) * softplus(float(a) + dt_bias)
+ * a, b: [T_total, Hv] in dtype with token stride ab_st (the in_proj_a /
+ * in_proj_b outputs); A_log, dt_bias: [Hv] f32.  Every other argument is as
+ * for gdn_chunk_prefill.  g and beta match the reference's torch expressions
+ * bit for bit, so the result equals gdn_chunk_prefill given those tensors.
+ */
+GDN_API int gdn_chunk_prefill_gates(const void* q, int64_t q_st, const void* k, int64_t k_st, const void* v,
+                                    int64_t v_st, const void* a, const void* b, int64_t ab_st,
+                                    const float* A_log, const float* dt_bias, const int32_t* cu_seqlens,
+                                    int B, int64_t T_total, const float* init_pool, const int32_t* init_slot,
+                                    const int32_t* use_initial, float* final_pool, const int32_t* final_slot,
+                                    int64_t n_slots, void* out, int64_t o_st, int Hk, int Hv, int dk, int dv,
+                                    int use_qk_l2norm, int dtype, int32_t* err_flag, void* stream);
+
+/* ---------------------------------------------------------------------------
  * Layer RMSNorm of the hybrid model, Qwen3_5RMSNorm.forward (transformers
  * modeling_qwen3_5.py): y = x * rsqrt(mean(x^2) + eps) * (1 + weight) in fp32,
  * rounded once to dtype; the norm the reference replaces with npu_rms_norm in

@@ -135,7 +135,11 @@ def chunk_gated_delta_rule(query, key, value, g, beta, chunk_size=64, initial_st
 
     query/key [B,L,H,dk], value [B,L,H,dv], g/beta [B,L,H] (float32 arrays holding values
     of dtype ``dt``; g is float32 in the reference).  Returns (out [B,L,H,dv] rounded to
-    ``dt``, final state [B,H,dk,dv] float32 or None)."""
+    ``dt``, final state [B,H,dk,dv] float32 or None).
+
+    L = 0 is defined as the zero-chunk limit (no output rows, final state = initial state or zeros);
+    the reference raises there (torch.stack of an empty chunk list, src/gdn_chunk_fast2.py:60), and
+    the library's packed prefill follows this definition for empty sequences."""
     q, k = np.asarray(query, F32), np.asarray(key, F32)
     if use_qk_l2norm_in_kernel:
         q = l2norm(q, dt)
@@ -175,7 +179,8 @@ def chunk_gated_delta_rule(query, key, value, g, beta, chunk_size=64, initial_st
         vn = V[:, :, i] - np.matmul(Kc[:, :, i], S)
         outs.append(np.matmul(Qg[:, :, i], S) + np.matmul(QK[:, :, i], vn))
         S = (S * Gl[:, :, i, None, None] + np.matmul(Kd[:, :, i], vn)).astype(F32)
-    core = np.stack(outs, axis=2).reshape(B, H, Lp, dv)[:, :, :L]
+    core = (np.stack(outs, axis=2).reshape(B, H, Lp, dv)[:, :, :L] if outs
+            else np.zeros((B, H, 0, dv), F32))
     out = rnd(np.swapaxes(core, 1, 2), dt)
     return out, (S if output_final_state else None)
 

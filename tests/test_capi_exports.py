@@ -59,6 +59,9 @@ def test_validation_errors_without_gpu(lib):
     rc = lib.gdn_chunk_prefill(None, 0, None, 0, None, 0, None, None, 0, None, 1, 10, None, None, None, None,
                                None, 0, None, 0, 16, 48, 128, 128, 1, 1, None, None)
     assert rc == 1 and b"null" in lib.gdn_last_error()
+    rc = lib.gdn_chunk_prefill_gates(None, 0, None, 0, None, 0, None, None, 0, None, None, None, 1, 10, None, None,
+                                     None, None, None, 0, None, 0, 16, 48, 128, 128, 1, 1, None, None)
+    assert rc == 1 and b"gdn_chunk_prefill_gates: null" in lib.gdn_last_error()
     rc = lib.gdn_recurrent(*([None, 0, 0] * 3), None, None, 0, 0, None, None, None, None, 0, None, 0, 0,
                            1, 1, 16, 40, 128, 128, 1, 1, None, None)
     assert rc == 2 and b"multiple" in lib.gdn_last_error()

@@ -296,6 +296,133 @@ def test_chunk_matches_token_recurrence_bf16(ops):
     assert (sc - sr).abs().max().item() < 2e-2
 
 
+@pytest.mark.parametrize("dd,dt", [(128, torch.bfloat16), (64, torch.float32)])
+def test_chunk_prefill_gates_matches_torch_gate_lines(ops, dd, dt):
+    """Gates formed in-kernel (chunk_prefill_varlen_gates) == the reference's torch gate lines
+    (src/cb_tp.py:170-171) fed to chunk_prefill_varlen: identical g and beta give identical results
+    (checked at the contract tolerance: bf16 2e-2 max-abs, fp32 1e-4 relative), slot placement bit for
+    bit; and the bf16 path against the oracle.  a includes values past softplus's threshold of 20."""
+    import torch.nn.functional as F
+    rng = np.random.default_rng(21)
+    lens, Hk, Hv = [70, 300, 1], 2, 6
+    Tt = sum(lens)
+    cu_h = np.array([0, lens[0], lens[0] + lens[1], Tt], np.int32)
+    q = rng.standard_normal((Tt, Hk, dd)).astype(np.float32)
+    k = rng.standard_normal((Tt, Hk, dd)).astype(np.float32)
+    v = rng.standard_normal((Tt, Hv, dd)).astype(np.float32)
+    a = (3 * rng.standard_normal((Tt, Hv))).astype(np.float32)
+    a[::17, 1] = 25.0
+    b = (2 * rng.standard_normal((Tt, Hv))).astype(np.float32)
+    if dt == torch.bfloat16:
+        q, k, v, a, b = (O.bf16(x) for x in (q, k, v, a, b))
+    A_log = O.bf16(np.log(rng.uniform(1, 16, Hv)))
+    dt_bias = O.bf16(rng.uniform(-1, 1, Hv))
+    pool0 = (0.02 * rng.standard_normal((5, Hv, dd, dd))).astype(np.float32)
+    slot_h = np.array([2, 0, 3], np.int32)
+    use_h = np.array([1, 0, 1], np.int32)
+    qd, kd, vd, ad, bd = T(q, dt), T(k, dt), T(v, dt), T(a, dt), T(b, dt)
+    Ad, dbd = T(A_log), T(dt_bias)
+    cu = torch.tensor(cu_h, device=DEV)
+    slot = torch.tensor(slot_h, device=DEV)
+    use = torch.tensor(use_h, device=DEV)
+    beta_t = bd.sigmoid().float()
+    g_t = -Ad.exp() * F.softplus(ad.float() + dbd)
+    pool_ref, pool_raw = T(pool0), T(pool0)
+    pool_raw[1] = float("nan")
+    pool_raw[4] = float("nan")
+    o_ref = ops.chunk_prefill_varlen(qd, kd, vd, g_t, beta_t, cu, pool_ref, slot, use, True)
+    o_raw = ops.chunk_prefill_varlen_gates(qd, kd, vd, ad, bd, Ad, dbd, cu, pool_raw, slot, use, True)
+    torch.cuda.synchronize()
+    assert torch.isnan(pool_raw[1]).all() and torch.isnan(pool_raw[4]).all()
+    sl = slot.long()
+    if dt == torch.bfloat16:
+        assert (o_raw.float() - o_ref.float()).abs().max().item() <= 2e-2
+        assert (pool_raw[sl] - pool_ref[sl]).abs().max().item() <= 2e-2
+        b_o, g_o = O.decode_gates(a, b, A_log, dt_bias, "bf16")
+        ref_pool = pool0.copy()
+        ro, _ = O.prefill_varlen(q, k, v, g_o, b_o, cu_h, ref_pool, slot_h, use_h, True, "bf16")
+        assert bf16_ok(N(o_raw), ro)
+        assert np.abs(N(pool_raw)[slot_h] - ref_pool[slot_h]).max() < 2e-2
+    else:
+        assert rel(N(o_raw), N(o_ref)) <= 1e-4
+        assert rel(N(pool_raw[sl]), N(pool_ref[sl])) <= 1e-4
+
+
+@pytest.mark.parametrize("dd,dt", [(128, torch.bfloat16), (64, torch.float32)])
+def test_chunk_prefill_empty_and_ragged_sequences(ops, dd, dt):
+    """Packed prefill with empty sequences between ragged ones (1, 64, 65, 127 tokens): outputs and
+    states match the oracle; an empty sequence's final state is its initial state (bit for bit) or
+    zeros; unused pool rows stay untouched.  A call whose sequences are all empty writes only states."""
+    rng = np.random.default_rng(22)
+    lens, Hk, Hv = [0, 65, 0, 1, 64, 127, 0], 1, 3
+    Tt = sum(lens)
+    cu_h = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    bfl = dt == torch.bfloat16
+    cast = O.bf16 if bfl else (lambda x: x.astype(np.float32))
+    q = cast(rng.standard_normal((Tt, Hk, dd)))
+    k = cast(rng.standard_normal((Tt, Hk, dd)))
+    v = cast(rng.standard_normal((Tt, Hv, dd)))
+    g = -rng.uniform(0.01, 1, (Tt, Hv)).astype(np.float32)
+    be = cast(rng.uniform(0, 1, (Tt, Hv)))
+    pool0 = (0.02 * rng.standard_normal((9, Hv, dd, dd))).astype(np.float32)
+    pool0[[0, 8]] = np.nan                                 # rows nobody uses
+    slot_h = np.arange(1, 8, dtype=np.int32)
+    use_h = np.array([1, 0, 0, 1, 0, 1, 0], np.int32)      # sequence 0 empty from a state, 2 and 6 from zeros
+    pool = T(pool0)
+    o = ops.chunk_prefill_varlen(T(q, dt), T(k, dt), T(v, dt), T(g), T(be), torch.tensor(cu_h, device=DEV), pool,
+                                 torch.tensor(slot_h, device=DEV), torch.tensor(use_h, device=DEV), True)
+    ref_pool = pool0.copy()
+    ro, _ = O.prefill_varlen(q, k, v, g, be, cu_h, ref_pool, slot_h, use_h, True, "bf16" if bfl else "f32")
+    got = N(pool)
+    assert o.shape == (Tt, Hv, dd)
+    if bfl:
+        assert bf16_ok(N(o), ro)
+        assert np.abs(got[slot_h] - ref_pool[slot_h]).max() < 2e-2
+    else:
+        assert rel(N(o), ro) < 1e-4
+        assert rel(got[slot_h], ref_pool[slot_h]) < 1e-4
+    assert np.array_equal(got[1], pool0[1])                # empty, initial state kept bit for bit
+    assert not got[3].any() and not got[7].any()           # empty, from zeros
+    assert np.isnan(got[0]).all() and np.isnan(got[8]).all()
+    # every sequence empty: no tokens, only states
+    pool2 = T(pool0)
+    e = torch.empty(0, Hk, dd, dtype=dt, device=DEV)
+    ev = torch.empty(0, Hv, dd, dtype=dt, device=DEV)
+    eg = torch.empty(0, Hv, device=DEV)
+    o2 = ops.chunk_prefill_varlen(e, e, ev, eg, eg, torch.zeros(4, dtype=torch.int32, device=DEV), pool2,
+                                  torch.tensor([1, 2, 3], dtype=torch.int32, device=DEV),
+                                  torch.tensor([1, 0, 1], dtype=torch.int32, device=DEV), True)
+    got2 = N(pool2)
+    assert o2.shape == (0, Hv, dd)
+    assert np.array_equal(got2[1], pool0[1]) and np.array_equal(got2[3], pool0[3]) and not got2[2].any()
+    assert np.array_equal(got2[4:8], pool0[4:8])
+
+
+def test_prefill_conv_empty_sequences(ops):
+    """Varlen prefill conv with empty sequences: an empty sequence keeps its carried conv state (or
+    gets zeros without one), bit for bit; the others match the oracle."""
+    rng = np.random.default_rng(23)
+    bf = torch.bfloat16
+    lens, C, K = [0, 3, 0, 5, 1], 256, 4
+    Tt = sum(lens)
+    cu_h = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    x = O.bf16(rng.standard_normal((Tt, C)))
+    w = O.bf16(rng.uniform(-0.5, 0.5, (C, K)))
+    pool0 = O.bf16(rng.standard_normal((len(lens) + 1, C, K)))
+    slot_h = np.array([5, 1, 2, 3, 4], np.int32)
+    use_h = np.array([1, 1, 0, 0, 1], np.int32)
+    pool = T(pool0, bf)
+    y = ops.prefill_conv_varlen(T(x, bf), torch.tensor(cu_h, device=DEV), T(w, bf), None, pool,
+                                torch.tensor(slot_h, device=DEV), torch.tensor(use_h, device=DEV))
+    init = np.where(use_h[:, None, None] != 0, pool0[slot_h], 0).astype(np.float32)
+    yr, st = O.prefill_conv(x, cu_h, w, None, init, "bf16")
+    assert bf16_ok(N(y), yr, atol=0)
+    got = N(pool)
+    assert np.array_equal(got[slot_h], st)
+    assert np.array_equal(got[5], pool0[5]) and not got[2].any()
+    assert np.array_equal(got[0], pool0[0])
+
+
 # ----------------------------------------------------------------------------- fused decode layer
 def test_rmsnorm_matches_hf_module(ops):
     """ops.rmsnorm == Qwen3_5RMSNorm.forward (fp32 statistics, x * r * (1 + w), one rounding) within one
