@@ -459,6 +459,10 @@ __global__ void __launch_bounds__(kNT, 1)
           cv.nt = nt;
         }
         if (nx.live) load_gates(nx);
+        // the next chunk opens a new item: start its initial state towards L2 now, a chunk or two before
+        // the recurrence group loads it into TMEM
+        if (lane == 0 && nx.live && nx.ci == 0 && nx.it.init)
+          bulk_prefetch_l2(p.init_pool + (nx.it.islot * p.Hv + nx.it.h) * int64_t(kD * kD), kD * kD * 4);
       }
       if (ok && !mbar_wait(bar_qk0 + 8 * bf, uint32_t(gc >> 1) & 1u)) ok = false;
       if (nt < kC) {  // zero the q/k rows past the sequence end (they hold the next sequence)
@@ -801,6 +805,9 @@ int run_chunk_tc(const ChunkParams& p, int64_t T_total, cudaStream_t s) {
       return fail(GDN_ERR_ARG, "gdn_chunk_prefill: q/k/v need 16-byte aligned bases and token strides "
                                "that are multiples of 8 elements");
   }
+  // the state rows move as 16-byte vectors (and are prefetched into L2 by bulk prefetches)
+  if (!aligned(p.init_pool, 16) || !aligned(p.final_pool, 16))
+    return fail(GDN_ERR_ARG, "gdn_chunk_prefill: init_pool / final_pool need 16-byte aligned bases");
   if (T_total >= (int64_t(1) << 31)) return fail(GDN_ERR_ARG, "gdn_chunk_prefill: T_total too large");
   CUtensorMap mq, mk, mv, mo;
   int rc = make_map(&mq, p.q, p.Hk, T_total, p.q_st);
