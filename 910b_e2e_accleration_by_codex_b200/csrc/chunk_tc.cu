@@ -234,6 +234,7 @@ struct ChunkVec {
   float egc[64];  // exp(gc)
   float dkd[64];  // rk exp(gl - gc)
   float bwc[64];  // beta exp(gc) rk
+  float osc[64];  // rq scale exp(gc): the output scale of S^T q_t
   float gl, Gl;   // log2-scaled total decay of the chunk and exp of it
   int nt;         // live tokens in the chunk
   int pad;
@@ -265,10 +266,12 @@ constexpr uint32_t W_BQK0 = 180224;    // QKm [t][s], buffer 0
 constexpr uint32_t W_BQK1 = 188416;    // buffer 1
 constexpr uint32_t W_X = 196608;       // fp32 64 x LT inverse scratch (17408 B) + 32 x LP merge scratch
 constexpr uint32_t W_VEC = 218624;     // 2 x ChunkVec
-constexpr uint32_t W_BAR = W_VEC + 2 * 2048;  // mbarriers
+constexpr uint32_t kVecBytes = 2304;   // one ChunkVec slot (16-byte multiple)
+constexpr uint32_t W_BAR = W_VEC + 2 * kVecBytes;  // mbarriers
 constexpr uint32_t W_ORD = W_BAR + 128;  // sequences ranked longest first (kSortMax ints)
 constexpr uint32_t W_SMEM = W_ORD + 4 * 256 + 1024;
-static_assert(sizeof(ChunkVec) <= 2048, "ChunkVec");
+static_assert(sizeof(ChunkVec) <= kVecBytes && kVecBytes % 16 == 0, "ChunkVec");
+static_assert(W_SMEM <= 232448, "dynamic shared memory above the 227 KB per-CTA limit");
 static_assert(W_X + 64 * LT * 4 + 32 * LP * 4 <= W_VEC, "scratch");
 
 // TMEM columns
@@ -426,7 +429,7 @@ __global__ void __launch_bounds__(kNT, 1)
     if (warp == 0 && cur.live) load_gates(cur);
     for (int gc = 0; cur.live; ++gc) {
       const int bf = gc & 1;
-      ChunkVec& cv = *reinterpret_cast<ChunkVec*>(sm + W_VEC + 2048 * bf);
+      ChunkVec& cv = *reinterpret_cast<ChunkVec*>(sm + W_VEC + kVecBytes * bf);
       const int64_t c0 = cur.it.s0 + int64_t(cur.ci) * kC, s1 = cur.it.s1;
       const int nt = int((s1 - c0) < kC ? (s1 - c0) : kC);
       uint8_t* qk = sm + (bf ? W_QK1 : W_QK0);
@@ -500,6 +503,7 @@ __global__ void __launch_bounds__(kNT, 1)
         const float rk = cv.rn[64 + tid];
         cv.dkd[tid] = rk * ex2(cv.gl - cv.gc[tid]);
         cv.bwc[tid] = cv.bt[tid] * cv.egc[tid] * rk;
+        cv.osc[tid] = cv.rn[tid] * scale * cv.egc[tid];
       }
       {  // P1 epilogue: QKm tile (rows 0-63) and X (rows 64-127), from the K columns 64-127
         {
@@ -510,18 +514,26 @@ __global__ void __launch_bounds__(kNT, 1)
             const int t = row;
             const float gt = cv.gc[t], f = cv.rn[t] * scale;
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const int s = 32 * half + j;
-              a[j] = (s <= t) ? a[j] * f * cv.rn[64 + s] * ex2(gt - cv.gc[s]) : 0.f;
+            for (int j4 = 0; j4 < 8; ++j4) {  // the per-column vectors as 16-byte broadcast loads
+              const float4 gs = lds4(cv.gc + 32 * half + 4 * j4), rs = lds4(cv.rn + 64 + 32 * half + 4 * j4);
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const int j = 4 * j4 + e, s = 32 * half + j;
+                a[j] = (s <= t) ? a[j] * f * f4get(rs, e) * ex2(gt - f4get(gs, e)) : 0.f;
+              }
             }
             store_row32(sm + bqk, 64, t, 4 * half, a);
           } else {
             const int i = row - 64;
             const float gi = cv.gc[i], f = cv.rn[64 + i] * cv.bt[i];
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const int s = 32 * half + j;
-              a[j] = (s < i) ? -(a[j] * f * cv.rn[64 + s]) * ex2(gi - cv.gc[s]) : 0.f;
+            for (int j4 = 0; j4 < 8; ++j4) {
+              const float4 gs = lds4(cv.gc + 32 * half + 4 * j4), rs = lds4(cv.rn + 64 + 32 * half + 4 * j4);
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const int j = 4 * j4 + e, s = 32 * half + j;
+                a[j] = (s < i) ? -(a[j] * f * f4get(rs, e)) * ex2(gi - f4get(gs, e)) : 0.f;
+              }
             }
             // 16-byte stores: lanes are rows LT floats apart, so scalar stores would hit 8 banks
 #pragma unroll
@@ -539,12 +551,12 @@ __global__ void __launch_bounds__(kNT, 1)
 #pragma unroll
         for (int e4 = 0; e4 < 4; ++e4) {
           const float4 tv4 = lds4(Xs + t * LT + cb + 4 * e4);
+          const float4 bt4 = lds4(cv.bt + cb + 4 * e4), bw4 = lds4(cv.bwc + cb + 4 * e4);
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            const int s = cb + 4 * e4 + e;
             const float tv = f4get(tv4, e);
-            u[4 * e4 + e] = tv * cv.bt[s];
-            w[4 * e4 + e] = tv * cv.bwc[s];
+            u[4 * e4 + e] = tv * f4get(bt4, e);
+            w[4 * e4 + e] = tv * f4get(bw4, e);
           }
         }
         store_row16(sm + W_BU, 64, t, cb >> 3, u);
@@ -624,7 +636,7 @@ __global__ void __launch_bounds__(kNT, 1)
     }
     for (int ci = 0; ci < itm.nch; ++ci, ++gc) {
       const int bf = gc & 1;
-      const ChunkVec& cv = *reinterpret_cast<const ChunkVec*>(sm + W_VEC + 2048 * bf);
+      const ChunkVec& cv = *reinterpret_cast<const ChunkVec*>(sm + W_VEC + kVecBytes * bf);
       const int64_t c0 = itm.s0 + int64_t(ci) * kC;
       const uint32_t qk_a = sb + (bf ? W_QK1 : W_QK0);
       const uint32_t bqk = bf ? W_BQK1 : W_BQK0;
@@ -672,7 +684,11 @@ __global__ void __launch_bounds__(kNT, 1)
           float a[32], d[32];
           tmem_ld32(tU + lane_off + 32 * half, a);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) d[j] = a[j] * cv.dkd[32 * half + j];
+          for (int j4 = 0; j4 < 8; ++j4) {
+            const float4 dk4 = lds4(cv.dkd + 32 * half + 4 * j4);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) d[4 * j4 + e] = a[4 * j4 + e] * f4get(dk4, e);
+          }
           store_row32(sm + W_VNT, 128, row, 4 * half, a);
           store_row32(sm + W_VND, 128, row, 4 * half, d);
         }
@@ -705,9 +721,13 @@ __global__ void __launch_bounds__(kNT, 1)
           tmem_ld32(tW + lane_off + 32 * half, a);
           tmem_ld32(tU + lane_off + 32 * half, c);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int t = 32 * half + j;
-            ot[t * kD + row] = __float2bfloat16_rn(a[j] * (cv.rn[t] * scale * cv.egc[t]) + c[j]);
+          for (int j4 = 0; j4 < 8; ++j4) {
+            const float4 os4 = lds4(cv.osc + 32 * half + 4 * j4);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int j = 4 * j4 + e, t = 32 * half + j;
+              ot[t * kD + row] = __float2bfloat16_rn(a[j] * f4get(os4, e) + c[j]);
+            }
           }
         }
       }
