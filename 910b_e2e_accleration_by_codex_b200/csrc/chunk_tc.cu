@@ -116,9 +116,10 @@ __device__ __forceinline__ void group_sync(int id) {
 // T = (I - X)^-1 for the strictly lower 64x64 X held in fp32 shared memory (row stride LT), in
 // place, by the blocked scheme of src/gdn_chunk_fast.py:33-62: 16x16 diagonal blocks by the row
 // recurrence (evaluated column-wise), then pairwise merges T21 = (B X21) A.  Run by the 8 warps of
-// the intra group (named barrier 1); P is 32 x LP floats of scratch.  In the merges a lane owns
-// one output column: the column operand is one conflict-free 32-bit load per row and the row
-// operand a uniform-address float4, which keeps the shared-memory wavefront count low.
+// the intra group (named barrier 1); P is 32 x LP floats of scratch.  In the products B X21 a lane
+// owns one output column: the column operand is one conflict-free 32-bit load per row and the row
+// operand a uniform-address float4; in the last product P A a lane owns one output row (P rows are
+// LP floats apart, so their 16-byte loads do not conflict) and the A rows are uniform-address.
 __device__ __forceinline__ void tri_inverse64(float* X, float* P, int warp, int lane) {
   if (warp < 4) {  // diagonal block `warp`; lane j < 16 owns column j
     const int b0 = 16 * warp, j = lane & 15;
@@ -155,12 +156,17 @@ __device__ __forceinline__ void tri_inverse64(float* X, float* P, int warp, int 
     }
   }
   group_sync(1);
+  // In both merge levels the first product B X21 has a lower-triangular left factor B, so the rows of
+  // row group g need only the first g + 1 four-column steps; the warps that share a scheduler (w and
+  // w + 4) take complementary row groups, which evens their work.  Skipped terms are exact zeros and
+  // the remaining ones are summed in the same ascending order, so the result does not change.
   {  // level 1: merge m = warp / 4 (blocks (0,1) or (2,3)), column c = lane % 16, rows r0, r0 + 1 with
-     // r0 = 4 (warp % 4) + 2 (lane / 16): the half-warps read the same column (a broadcast)
-    const int m = warp >> 2, c = lane & 15, lo = m * 32, hi = lo + 16, r0 = 4 * (warp & 3) + 2 * (lane >> 4);
+     // r0 = 4 rg + 2 (lane / 16), rg = warp % 4 (merge 0) or 3 - warp % 4 (merge 1): the half-warps
+     // read the same column (a broadcast)
+    const int m = warp >> 2, c = lane & 15, lo = m * 32, hi = lo + 16;
+    const int rg = m == 0 ? (warp & 3) : 3 - (warp & 3), r0 = 4 * rg + 2 * (lane >> 4);
     float a[2] = {0.f, 0.f};
-#pragma unroll
-    for (int tq = 0; tq < 4; ++tq) {
+    for (int tq = 0; tq <= rg; ++tq) {  // B = T(hi, hi) is lower triangular: columns < 4 (rg + 1)
       float x[4];
 #pragma unroll
       for (int u = 0; u < 4; ++u) x[u] = lds1(X + (hi + 4 * tq + u) * LT + lo + c);
@@ -190,38 +196,44 @@ __device__ __forceinline__ void tri_inverse64(float* X, float* P, int warp, int 
     for (int rr = 0; rr < 2; ++rr) X[(hi + r0 + rr) * LT + lo + c] = a[rr];
     group_sync(1);
   }
-  {  // level 2: column c = lane, rows 4w .. 4w+3
-    const int c = lane, r0 = 4 * warp;
-    float a[4] = {0.f, 0.f, 0.f, 0.f};
+  {  // level 2: group g = warp (warps 0-3) or 11 - warp (warps 4-7)
+    const int g = warp < 4 ? warp : 11 - warp;
+    {  // P = T(32:64, 32:64) X(32:64, 0:32): column c = lane, rows 4g .. 4g+3, columns of B below 4 (g + 1)
+      const int c = lane, r0 = 4 * g;
+      float a[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int tq = 0; tq <= g; ++tq) {
+        float x[4];
 #pragma unroll
-    for (int tq = 0; tq < 8; ++tq) {
-      float x[4];
+        for (int u = 0; u < 4; ++u) x[u] = lds1(X + (32 + 4 * tq + u) * LT + c);
 #pragma unroll
-      for (int u = 0; u < 4; ++u) x[u] = lds1(X + (32 + 4 * tq + u) * LT + c);
-#pragma unroll
-      for (int rr = 0; rr < 4; ++rr) {
-        const float4 bv = lds4(X + (32 + r0 + rr) * LT + 32 + 4 * tq);
-        a[rr] = fmaf(bv.w, x[3], fmaf(bv.z, x[2], fmaf(bv.y, x[1], fmaf(bv.x, x[0], a[rr]))));
+        for (int rr = 0; rr < 4; ++rr) {
+          const float4 bv = lds4(X + (32 + r0 + rr) * LT + 32 + 4 * tq);
+          a[rr] = fmaf(bv.w, x[3], fmaf(bv.z, x[2], fmaf(bv.y, x[1], fmaf(bv.x, x[0], a[rr]))));
+        }
       }
-    }
 #pragma unroll
-    for (int rr = 0; rr < 4; ++rr) P[(r0 + rr) * LP + c] = a[rr];
+      for (int rr = 0; rr < 4; ++rr) P[(r0 + rr) * LP + c] = a[rr];
+    }
     group_sync(1);
+    {  // T(32:64, 0:32) = P T(0:32, 0:32): row r = lane, columns 4g .. 4g+3; T(0:32, 0:32) is lower
+       // triangular, so only k >= 4g contribute.  P rows are 36 floats apart (conflict-free 16-byte
+       // loads), the T rows are uniform across the warp (broadcast), the result leaves as one 16-byte store.
+      const int r = lane, c0 = 4 * g;
+      float b[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int k4 = g; k4 < 8; ++k4) {
+        const float4 pv = lds4(P + r * LP + 4 * k4);
 #pragma unroll
-    for (int rr = 0; rr < 4; ++rr) a[rr] = 0.f;
-#pragma unroll
-    for (int tq = 0; tq < 8; ++tq) {
-      float x[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) x[u] = lds1(X + (4 * tq + u) * LT + c);
-#pragma unroll
-      for (int rr = 0; rr < 4; ++rr) {
-        const float4 pv = lds4(P + (r0 + rr) * LP + 4 * tq);
-        a[rr] = fmaf(pv.w, x[3], fmaf(pv.z, x[2], fmaf(pv.y, x[1], fmaf(pv.x, x[0], a[rr]))));
+        for (int u = 0; u < 4; ++u) {
+          const float4 tv = lds4(X + (4 * k4 + u) * LT + c0);
+          const float pk = f4get(pv, u);
+          b[0] = fmaf(pk, tv.x, b[0]);
+          b[1] = fmaf(pk, tv.y, b[1]);
+          b[2] = fmaf(pk, tv.z, b[2]);
+          b[3] = fmaf(pk, tv.w, b[3]);
+        }
       }
+      *reinterpret_cast<float4*>(X + (32 + r) * LT + c0) = make_float4(b[0], b[1], b[2], b[3]);
     }
-#pragma unroll
-    for (int rr = 0; rr < 4; ++rr) X[(32 + r0 + rr) * LT + c] = a[rr];
     group_sync(1);
   }
 }
