@@ -725,20 +725,36 @@ __global__ void __launch_bounds__(kNT, 1)
       if (ok && !mbar_wait(bar_mr, ph_mr)) ok = false;
       ph_mr ^= 1u;
       tc_fence_after();
-      {  // output o[t][v] = rq_t scale e^gc_t (S^T q_t)[v] + (vn^T QKm^T)[v][t] -> staging (W_WT)
-        __nv_bfloat16* ot = reinterpret_cast<__nv_bfloat16*>(sm + W_WT);
+      {  // output o[t][v] = rq_t scale e^gc_t (S^T q_t)[v] + (vn^T QKm^T)[v][t] -> staging (W_WT), laid out as
+         // the two 128-byte-swizzled 64 x 64 boxes of the output tensor map.  The 16x256b TMEM loads give
+         // this thread (v, t..t+1) pairs of 8 x 8 blocks (rows v, columns t), which stmatrix.trans writes as
+         // 16-byte rows of t holding 8 consecutive v: 8 stores per thread and chunk instead of 64.
+        const int g = lane >> 2, qd = lane & 3, m = lane >> 3, kr = lane & 7;
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
-          float a[32], c[32];
-          tmem_ld32(tW + lane_off + 32 * half, a);
-          tmem_ld32(tU + lane_off + 32 * half, c);
+          float2 os[4];
 #pragma unroll
-          for (int j4 = 0; j4 < 8; ++j4) {
-            const float4 os4 = lds4(cv.osc + 32 * half + 4 * j4);
+          for (int j = 0; j < 4; ++j) os[j] = *reinterpret_cast<const float2*>(cv.osc + 32 * half + 8 * j + 2 * qd);
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int j = 4 * j4 + e, t = 32 * half + j;
-              ot[t * kD + row] = __float2bfloat16_rn(a[j] * f4get(os4, e) + c[j]);
+          for (int lg = 0; lg < 2; ++lg) {  // TMEM lanes (v) 32 wg + 16 lg .. + 15
+            const uint32_t loff = uint32_t(32 * wg + 16 * lg) << 16;
+            uint32_t a[16], c[16];
+            tmem_ld16x256_x4(tW + loff + 32 * half, a);
+            tmem_ld16x256_x4(tU + loff + 32 * half, c);
+            tmem_ld_wait();
+            uint32_t pk[8];  // pk[2j + vb]: v = 32 wg + 16 lg + 8 vb + g, t = 32 half + 8 j + 2 qd, +1
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+#pragma unroll
+              for (int vb = 0; vb < 2; ++vb)
+                pk[2 * j + vb] = pack2(__uint_as_float(a[4 * j + 2 * vb]) * os[j].x + __uint_as_float(c[4 * j + 2 * vb]),
+                                       __uint_as_float(a[4 * j + 2 * vb + 1]) * os[j].y +
+                                           __uint_as_float(c[4 * j + 2 * vb + 1]));
+#pragma unroll
+            for (int jj = 0; jj < 2; ++jj) {  // matrices (j, vb) = (2jj, 0), (2jj, 1), (2jj+1, 0), (2jj+1, 1)
+              const int t = 32 * half + 8 * (2 * jj + (m >> 1)) + kr, v0 = 32 * wg + 16 * lg + 8 * (m & 1);
+              stmatrix_x4_trans(sb + W_WT + chunk_off(t, v0 >> 3, 64), pk[4 * jj], pk[4 * jj + 1], pk[4 * jj + 2],
+                                pk[4 * jj + 3]);
             }
           }
         }
@@ -749,6 +765,7 @@ __global__ void __launch_bounds__(kNT, 1)
       if (use_tma_store && nt == kC) {
         if (rt == 0) {
           tma_store_3d(&to, sb + W_WT, 0, h, int(c0));
+          tma_store_3d(&to, sb + W_WT + 8192, 64, h, int(c0));
           bulk_commit();
         }
       } else {
@@ -759,7 +776,7 @@ __global__ void __launch_bounds__(kNT, 1)
           const int cidx = rt + 128 * k8, t = cidx >> 4, cc = cidx & 15;
           if (t < nt)
             *reinterpret_cast<uint4*>(og + (c0 + t) * p.o_st + cc * 8) =
-                *reinterpret_cast<const uint4*>(ot + t * 256 + cc * 16);
+                *reinterpret_cast<const uint4*>(ot + chunk_off(t, cc, 64));
         }
       }
       group_sync(2);
@@ -811,16 +828,16 @@ static EncodeTiledFn encode_fn() {
 
 // 3-D map over a [T, H, 128] bf16 tensor with token stride `tok_stride` elements; box = 64 dims x
 // 1 head x 64 tokens, 128-byte swizzle (the UMMA canonical layout), zero fill out of bounds.
-static int make_map(CUtensorMap* m, const void* base, int H, int64_t T, int64_t tok_stride, bool store = false) {
+static int make_map(CUtensorMap* m, const void* base, int H, int64_t T, int64_t tok_stride) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return fail(GDN_ERR_CUDA, "gdn_chunk_prefill: cuTensorMapEncodeTiled unavailable");
   cuuint64_t dims[3] = {cuuint64_t(kD), cuuint64_t(H), cuuint64_t(T)};
   cuuint64_t strides[2] = {cuuint64_t(kD) * 2, cuuint64_t(tok_stride) * 2};
-  // loads: 64-element inner box with the 128-byte swizzle; the output store: a dense 128 x 64 box
-  cuuint32_t box[3] = {store ? 128u : 64u, 1, 64};
+  // loads and the output store: 64-element inner box (one token row half) x 64 tokens, 128-byte swizzle
+  cuuint32_t box[3] = {64u, 1, 64};
   cuuint32_t es[3] = {1, 1, 1};
   CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, es,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, store ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(GDN_ERR_CUDA, "gdn_chunk_prefill: tensor map encode failed (%d)", int(r));
   return GDN_OK;
@@ -848,7 +865,7 @@ int run_chunk_tc(const ChunkParams& p, int64_t T_total, cudaStream_t s) {
   if (rc) return rc;
   // full output chunks leave through a TMA store when the output rows allow one
   int use_store = aligned(p.out, 16) && (p.o_st % 8) == 0 && T_total > 0;
-  if (use_store && make_map(&mo, p.out, p.Hv, T_total, p.o_st, true) != GDN_OK) use_store = 0;
+  if (use_store && make_map(&mo, p.out, p.Hv, T_total, p.o_st) != GDN_OK) use_store = 0;
   if (!use_store) mo = mq;  // never read
   static bool attr_set[64] = {};
   static int sm_count[64] = {};
