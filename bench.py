@@ -453,9 +453,11 @@ def run_model(args, world, rank, local):
     lens = torch.randint(MODEL_PLEN[0], MODEL_PLEN[1] + 1, (slots,), generator=g).tolist()
     prompts = [torch.randint(0, MODEL_TEXT_CONFIG["vocab_size"], (1, L), generator=g) for L in lens]
     build_s = time.time() - t_build
-    # warm-up prefill (cuBLAS heuristics, allocator), then the timed packed prefill of every slot
-    eng.prefill_batch([0], [prompts[0][:, :64]])
-    eng.free(0)
+    # warm-up: the same packed prefill (GEMM shapes, cuBLAS heuristics and kernel loading, allocator),
+    # slots freed again; then the timed packed prefill of every slot
+    eng.prefill_batch(list(range(slots)), prompts)
+    for s_ in range(slots):
+        eng.free(s_)
     torch.cuda.synchronize()
     barrier(world)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
