@@ -426,13 +426,34 @@ __global__ void __launch_bounds__(kNT, 1)
   if (grp == 0) {
     // ======================================================================== intra-chunk group
     uint32_t ph_mi = 0;
-    float pg0 = 0.f, pg1 = 0.f, pb0 = 0.f, pb1 = 0.f;
+    // A chunk's gate inputs are loaded one chunk ahead into registers and used at the top of their
+    // chunk: g and beta as given, or in the raw-gate form in_proj_a / in_proj_b's outputs with the
+    // head's A_log and dt_bias (the raw-gate maths waits for the loads, so it runs at the top too).
+    float pg0 = 0.f, pg1 = 0.f, pb0 = 0.f, pb1 = 0.f, pA = 0.f, pD = 0.f;
     auto load_gates = [&](const Cur& x) {
       const int64_t c0 = x.it.s0 + int64_t(x.ci) * kC, s1 = x.it.s1;
       const int t0 = 2 * lane, t1 = 2 * lane + 1, h = x.it.h;
+      const int64_t i0 = (c0 + t0) * p.gb_st + h, i1 = (c0 + t1) * p.gb_st + h;
+      const bool l0 = c0 + t0 < s1, l1 = c0 + t1 < s1;
       pg0 = pg1 = pb0 = pb1 = 0.f;
-      if (c0 + t0 < s1) chunk_gate(p, c0 + t0, h, pg0, pb0);
-      if (c0 + t1 < s1) chunk_gate(p, c0 + t1, h, pg1, pb1);
+      if (p.a_raw == nullptr) {
+        if (l0) { pg0 = p.g[i0]; pb0 = p.beta[i0]; }
+        if (l1) { pg1 = p.g[i1]; pb1 = p.beta[i1]; }
+      } else {
+        pA = p.A_log[h];
+        pD = p.dt_bias[h];
+        if (p.raw_bf16) {
+          const __nv_bfloat16* ar = static_cast<const __nv_bfloat16*>(p.a_raw);
+          const __nv_bfloat16* br = static_cast<const __nv_bfloat16*>(p.b_raw);
+          if (l0) { pg0 = __bfloat162float(ar[i0]); pb0 = __bfloat162float(br[i0]); }
+          if (l1) { pg1 = __bfloat162float(ar[i1]); pb1 = __bfloat162float(br[i1]); }
+        } else {
+          const float* ar = static_cast<const float*>(p.a_raw);
+          const float* br = static_cast<const float*>(p.b_raw);
+          if (l0) { pg0 = ar[i0]; pb0 = br[i0]; }
+          if (l1) { pg1 = ar[i1]; pb1 = br[i1]; }
+        }
+      }
     };
     Cur cur, nx;
     seek(cur, 0);
@@ -452,6 +473,14 @@ __global__ void __launch_bounds__(kNT, 1)
       tc_fence_after();
       if (warp == 0) {  // gates: gc = cumsum(g) (log2-scaled), beta; prefetch the next chunk's
         const int t0 = 2 * lane, t1 = 2 * lane + 1;
+        if (p.a_raw != nullptr) {  // g = -exp(A_log) softplus(a + dt_bias), beta = sigmoid(b); 0 past the end
+          const float A = expf(pA);
+          const float s0 = sigmoid_f(pb0), s1 = sigmoid_f(pb1);
+          pg0 = t0 < nt ? -A * softplus_f(pg0 + pD) : 0.f;
+          pg1 = t1 < nt ? -A * softplus_f(pg1 + pD) : 0.f;
+          pb0 = t0 < nt ? (p.raw_bf16 ? bf16r(s0) : s0) : 0.f;
+          pb1 = t1 < nt ? (p.raw_bf16 ? bf16r(s1) : s1) : 0.f;
+        }
         const float g0 = pg0 * kLog2e, g1 = pg1 * kLog2e;
         cv.bt[t0] = pb0;
         cv.bt[t1] = pb1;
