@@ -268,10 +268,8 @@ struct Cur {
 constexpr uint32_t W_QK0 = 0;          // QK stage 0: [Q d0-63 | K d0-63 | Q d64-127 | K d64-127]
 constexpr uint32_t W_QK1 = 32768;      // QK stage 1
 constexpr uint32_t W_V = 65536;        // V [s][v] (single buffer; intra group only)
-constexpr uint32_t W_S16 = 81920;      // S bf16 [k][v] (recurrence group)
-constexpr uint32_t W_WT = 114688;      // W^T [k][t]; then the output staging o [t][v]
-constexpr uint32_t W_VNT = 131072;     // vn^T [v][s]
-constexpr uint32_t W_VND = 147456;     // (vn . d)^T [v][s]
+constexpr uint32_t W_WT = 81920;       // W^T [k][t]; then the output staging o [t][v]
+constexpr uint32_t W_INIT = 98304;     // the next item's initial state S [k][v] fp32 (64 KiB, bulk-loaded)
 constexpr uint32_t W_BU = 163840;      // T diag(beta) [t][s]
 constexpr uint32_t W_BW = 172032;      // T diag(beta e^gc rk) [t][s]
 constexpr uint32_t W_BQK0 = 180224;    // QKm [t][s], buffer 0
@@ -287,10 +285,15 @@ static_assert(W_SMEM <= 232448, "dynamic shared memory above the 227 KB per-CTA 
 static_assert(W_X + 64 * LT * 4 + 32 * LP * 4 <= W_VEC, "scratch");
 
 // TMEM columns
-constexpr uint32_t T_S = 0;      // state, 128 columns
-constexpr uint32_t T_P1 = 128;   // [Q;K][Q;K]^T, 128 columns (intra group)
-constexpr uint32_t T_U0 = 256;   // U^T -> vn^T -> vn^T QKm^T, 64 columns per buffer
-constexpr uint32_t T_W0 = 384;   // W^T -> S^T Q^T, 64 columns per buffer
+// TMEM columns.  The state is held transposed, S^T (lane v, column k), so that S^T and the vn^T tiles
+// (lane v as well) feed the recurrence group's MMAs as A operands straight from TMEM.
+constexpr uint32_t T_S = 0;      // S^T fp32, 128 columns
+constexpr uint32_t T_S16 = 128;  // S^T bf16 (A of P4, P5), 64 columns
+constexpr uint32_t T_VN16 = 192; // vn^T bf16 (A of vn^T QKm^T), 32 columns
+constexpr uint32_t T_VND = 224;  // (vn . rk e^(gl-gc))^T bf16 (A of P6), 32 columns
+constexpr uint32_t T_UW = 256;   // per buffer b (128 b + 256): U^T -> vn^T -> vn^T QKm^T (64 columns),
+                                 // then W^T -> S^T Q^T (64 columns); [Q;K][Q;K]^T of the intra group's
+                                 // chunk occupies the same 128 columns before P2/P3 overwrite them
 
 __global__ void __launch_bounds__(kNT, 1)
     chunk_tc_kernel(const ChunkParams p, const __grid_constant__ CUtensorMap tq,
@@ -307,6 +310,7 @@ __global__ void __launch_bounds__(kNT, 1)
   const uint32_t bar_qk0 = smem_u32(&bars[0]), bar_v = smem_u32(&bars[2]);
   const uint32_t bar_mi = smem_u32(&bars[3]), bar_mr = smem_u32(&bars[4]);
   const uint32_t bar_ready0 = smem_u32(&bars[5]), bar_free0 = smem_u32(&bars[7]);
+  const uint32_t bar_init = smem_u32(&bars[9]);  // the next item's initial state landed in W_INIT
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int grp = warp >= 8 ? 1 : 0;  // 0: intra-chunk group (warps 0-7), 1: recurrence group (8-11)
@@ -394,7 +398,7 @@ __global__ void __launch_bounds__(kNT, 1)
   };
 
   if (tid == 0) {
-    for (int i = 0; i < 9; ++i) mbar_init(smem_u32(&bars[i]), 1);
+    for (int i = 0; i < 10; ++i) mbar_init(smem_u32(&bars[i]), 1);
     fence_mbar_init();
     prefetch_tmap(&tq);
     prefetch_tmap(&tk);
@@ -523,7 +527,7 @@ __global__ void __launch_bounds__(kNT, 1)
         const uint32_t id = make_idesc(128, 128, false, false);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
-          umma(tmem + T_P1, desc_kmajor(qk_a, 128, kk), desc_kmajor(qk_a, 128, kk), id, kk > 0);
+          umma(tmem + T_UW + 128 * bf, desc_kmajor(qk_a, 128, kk), desc_kmajor(qk_a, 128, kk), id, kk > 0);
         umma_commit(bar_mi);
       }
       if (ok && !mbar_wait(bar_mi, ph_mi)) ok = false;
@@ -531,7 +535,7 @@ __global__ void __launch_bounds__(kNT, 1)
       tc_fence_after();
       if (hv == 0) {  // l2-norm factors from the diagonal (bf16 arithmetic as the reference's l2norm)
         float dg[32];
-        tmem_ld32(tmem + T_P1 + lane_off + 32 * wg, dg);
+        tmem_ld32(tmem + T_UW + 128 * bf + lane_off + 32 * wg, dg);
         float ss = dg[0];
 #pragma unroll
         for (int j = 1; j < 32; ++j) ss = j == lane ? dg[j] : ss;
@@ -550,7 +554,7 @@ __global__ void __launch_bounds__(kNT, 1)
         {
           const int half = hv;
           float a[32];
-          tmem_ld32(tmem + T_P1 + lane_off + 64 + 32 * half, a);
+          tmem_ld32(tmem + T_UW + 128 * bf + lane_off + 64 + 32 * half, a);
           if (row < 64) {
             const int t = row;
             const float gt = cv.gc[t], f = cv.rn[t] * scale;
@@ -618,10 +622,10 @@ __global__ void __launch_bounds__(kNT, 1)
         const uint32_t id = make_idesc(128, 64, true, false);
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
-          umma(tmem + T_U0 + 64 * bf, desc_mnmajor(sb + W_V, 64, kk), desc_kmajor(sb + W_BU, 64, kk), id, kk > 0);
+          umma(tmem + T_UW + 128 * bf, desc_mnmajor(sb + W_V, 64, kk), desc_kmajor(sb + W_BU, 64, kk), id, kk > 0);
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
-          umma(tmem + T_W0 + 64 * bf, desc_mnmajor(qk_a + 8192, 128, kk), desc_kmajor(sb + W_BW, 64, kk), id,
+          umma(tmem + T_UW + 128 * bf + 64, desc_mnmajor(qk_a + 8192, 128, kk), desc_kmajor(sb + W_BW, 64, kk), id,
                kk > 0);
         umma_commit(bar_mi);
       }
@@ -648,6 +652,22 @@ __global__ void __launch_bounds__(kNT, 1)
     step(q2);
     step(q2);
     int gc = 0;
+    uint32_t ph_init = 0;
+    // The initial states of this CTA's items arrive by one 64 KiB bulk copy each into W_INIT, in item
+    // order and one at a time: the copy for the next item that reads one is issued as soon as the
+    // current one has been moved into TMEM.
+    auto issue_init = [&](int k0) {  // thread rt == 0
+      ItemInfo nx;
+      for (int k = k0; item(k, nx); ++k) {
+        if (nx.ok && nx.init) {
+          fence_async_smem();  // the generic reads of the previous state are ordered before the copy
+          mbar_expect_tx(bar_init, kD * kD * 4);
+          bulk_load(sb + W_INIT, p.init_pool + (nx.islot * p.Hv + nx.h) * int64_t(kD * kD), kD * kD * 4, bar_init);
+          return;
+        }
+      }
+    };
+    if (rt == 0) issue_init(0);
     ItemInfo itm;
     for (int k = 0; item(k, itm); ++k) {
     if (!itm.ok) {  // a bad slot index: record it and leave every pool row untouched
@@ -655,25 +675,24 @@ __global__ void __launch_bounds__(kNT, 1)
       continue;
     }
     const int h = itm.h;
-    {  // initial state -> TMEM (thread: row k, all 128 columns)
-      float v[32];
+    {  // initial state -> TMEM as S^T: thread v (TMEM lane) takes column v of S [k][v] (conflict-free)
+      if (itm.init) {
+        if (ok && !mbar_wait(bar_init, ph_init)) ok = false;
+        ph_init ^= 1u;
+      }
+      const float* st = reinterpret_cast<const float*>(sm + W_INIT);
 #pragma unroll
       for (int part = 0; part < 4; ++part) {
-        if (itm.init) {
-          const float4* src = reinterpret_cast<const float4*>(p.init_pool + (itm.islot * p.Hv + h) * int64_t(kD * kD) +
-                                                              int64_t(row) * kD + 32 * part);
+        float v[32];
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const float4 f = src[i];
-            v[4 * i] = f.x; v[4 * i + 1] = f.y; v[4 * i + 2] = f.z; v[4 * i + 3] = f.w;
-          }
-        } else {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = 0.f;
-        }
+        for (int i = 0; i < 32; ++i) v[i] = itm.init ? st[(32 * part + i) * kD + row] : 0.f;
         tmem_st32(tmem + T_S + lane_off + 32 * part, v);
       }
       tmem_st_wait();
+      if (itm.init) {
+        group_sync(2);
+        if (rt == 0) issue_init(k + 1);
+      }
     }
     for (int ci = 0; ci < itm.nch; ++ci, ++gc) {
       const int bf = gc & 1;
@@ -681,7 +700,7 @@ __global__ void __launch_bounds__(kNT, 1)
       const int64_t c0 = itm.s0 + int64_t(ci) * kC;
       const uint32_t qk_a = sb + (bf ? W_QK1 : W_QK0);
       const uint32_t bqk = bf ? W_BQK1 : W_BQK0;
-      const uint32_t tU = tmem + T_U0 + 64 * bf, tW = tmem + T_W0 + 64 * bf;
+      const uint32_t tU = tmem + T_UW + 128 * bf, tW = tU + 64;
       if (ok && !mbar_wait(bar_ready0 + 8 * bf, uint32_t(gc >> 1) & 1u)) ok = false;
       tc_fence_after();
       if (rt == 0) bulk_wait_read();  // the previous chunk's output store has left W_WT
@@ -693,7 +712,10 @@ __global__ void __launch_bounds__(kNT, 1)
         for (int part = 0; part < 4; ++part) {
           float sv[32];
           tmem_ld32(tmem + T_S + lane_off + 32 * part, sv);
-          store_row32(sm + W_S16, 128, row, 4 * part, sv);
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) pk[i] = pack2(sv[2 * i], sv[2 * i + 1]);
+          tmem_st16u(tmem + T_S16 + lane_off + 16 * part, pk);
 #pragma unroll
           for (int j = 0; j < 32; ++j) sv[j] *= Gl;
           tmem_st32(tmem + T_S + lane_off + 32 * part, sv);
@@ -711,9 +733,9 @@ __global__ void __launch_bounds__(kNT, 1)
       group_sync(2);
       if (rt == 0) {  // P4: vn^T = U^T - S^T W^T
         tc_fence_after();
-        const uint32_t id = make_idesc(128, 64, true, true, true);
+        const uint32_t id = make_idesc(128, 64, false, true, true);
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) umma(tU, desc_mnmajor(sb + W_S16, 128, kk), desc_mnmajor(sb + W_WT, 128, kk), id, 1);
+        for (int kk = 0; kk < 8; ++kk) umma_ts(tU, tmem + T_S16 + 8 * kk, desc_mnmajor(sb + W_WT, 128, kk), id, 1);
         umma_commit(bar_mr);
       }
       if (ok && !mbar_wait(bar_mr, ph_mr)) ok = false;
@@ -730,25 +752,30 @@ __global__ void __launch_bounds__(kNT, 1)
 #pragma unroll
             for (int e = 0; e < 4; ++e) d[4 * j4 + e] = a[4 * j4 + e] * f4get(dk4, e);
           }
-          store_row32(sm + W_VNT, 128, row, 4 * half, a);
-          store_row32(sm + W_VND, 128, row, 4 * half, d);
+          uint32_t pa[16], pd[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            pa[i] = pack2(a[2 * i], a[2 * i + 1]);
+            pd[i] = pack2(d[2 * i], d[2 * i + 1]);
+          }
+          tmem_st16u(tmem + T_VN16 + lane_off + 16 * half, pa);
+          tmem_st16u(tmem + T_VND + lane_off + 16 * half, pd);
         }
+        tmem_st_wait();
       }
       fence_async_smem();
       tc_fence_before();
       group_sync(2);
-      if (rt == 0) {  // P5: W = S^T Q^T, U = vn^T QKm^T;  P6: S += K^T (vn . d)
+      if (rt == 0) {  // P5: W = S^T Q^T, U = vn^T QKm^T;  P6: S^T += (vn . d)^T K  (A operands from TMEM)
         tc_fence_after();
-        const uint32_t ia = make_idesc(128, 64, true, false);
+        const uint32_t ia = make_idesc(128, 64, false, false);
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) umma(tW, desc_mnmajor(sb + W_S16, 128, kk), desc_kmajor(qk_a, 128, kk), ia, kk > 0);
-        const uint32_t ib = make_idesc(128, 64, false, false);
+        for (int kk = 0; kk < 8; ++kk) umma_ts(tW, tmem + T_S16 + 8 * kk, desc_kmajor(qk_a, 128, kk), ia, kk > 0);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) umma(tU, desc_kmajor(sb + W_VNT, 128, kk), desc_kmajor(sb + bqk, 64, kk), ib, kk > 0);
-        const uint32_t ic = make_idesc(128, 128, true, false);
+        for (int kk = 0; kk < 4; ++kk) umma_ts(tU, tmem + T_VN16 + 8 * kk, desc_kmajor(sb + bqk, 64, kk), ia, kk > 0);
+        const uint32_t ic = make_idesc(128, 128, false, true);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          umma(tmem + T_S, desc_mnmajor(qk_a + 8192, 128, kk), desc_kmajor(sb + W_VND, 128, kk), ic, 1);
+        for (int kk = 0; kk < 4; ++kk) umma_ts(tmem + T_S, tmem + T_VND + 8 * kk, desc_mnmajor(qk_a + 8192, 128, kk), ic, 1);
         umma_commit(bar_mr);
       }
       if (ok && !mbar_wait(bar_mr, ph_mr)) ok = false;
@@ -758,7 +785,7 @@ __global__ void __launch_bounds__(kNT, 1)
          // the two 128-byte-swizzled 64 x 64 boxes of the output tensor map.  The 16x256b TMEM loads give
          // this thread (v, t..t+1) pairs of 8 x 8 blocks (rows v, columns t), which stmatrix.trans writes as
          // 16-byte rows of t holding 8 consecutive v: 8 stores per thread and chunk instead of 64.
-        const int g = lane >> 2, qd = lane & 3, m = lane >> 3, kr = lane & 7;
+        const int qd = lane & 3, m = lane >> 3, kr = lane & 7;
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
           float2 os[4];
@@ -818,16 +845,15 @@ __global__ void __launch_bounds__(kNT, 1)
       }
       step(q2);
     }
-    // final state
+    // final state: thread v holds column v of S; a warp's store of row k covers 128 contiguous bytes
     if (p.final_pool) {
+      float* dst = p.final_pool + (itm.fslot * p.Hv + h) * int64_t(kD * kD) + row;
 #pragma unroll
       for (int part = 0; part < 4; ++part) {
         float v[32];
         tmem_ld32(tmem + T_S + lane_off + 32 * part, v);
-        float4* dst = reinterpret_cast<float4*>(p.final_pool + (itm.fslot * p.Hv + h) * int64_t(kD * kD) +
-                                                int64_t(row) * kD + 32 * part);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+        for (int i = 0; i < 32; ++i) dst[(32 * part + i) * kD] = v[i];
       }
     }
     }
