@@ -781,6 +781,12 @@ __global__ void __launch_bounds__(kNT, 1)
       if (ok && !mbar_wait(bar_mr, ph_mr)) ok = false;
       ph_mr ^= 1u;
       tc_fence_after();
+      // P5/P6 were the last readers of this chunk's Q/K stage: refill it with chunk gc+2 now, ahead of
+      // the output epilogue and store
+      if (rt == 0 && q2.live) {
+        fence_async_smem();
+        issue_qk(q2, gc + 2);
+      }
       {  // output o[t][v] = rq_t scale e^gc_t (S^T q_t)[v] + (vn^T QKm^T)[v][t] -> staging (W_WT), laid out as
          // the two 128-byte-swizzled 64 x 64 boxes of the output tensor map.  The 16x256b TMEM loads give
          // this thread (v, t..t+1) pairs of 8 x 8 blocks (rows v, columns t), which stmatrix.trans writes as
@@ -836,13 +842,7 @@ __global__ void __launch_bounds__(kNT, 1)
         }
       }
       group_sync(2);
-      if (rt == 0) {  // chunk gc is done with its buffer set: prefetch chunk gc+2 into it, free it
-        if (q2.live) {
-          fence_async_smem();
-          issue_qk(q2, gc + 2);
-        }
-        mbar_arrive(bar_free0 + 8 * bf);
-      }
+      if (rt == 0) mbar_arrive(bar_free0 + 8 * bf);  // chunk gc is done with its buffer set: free it
       step(q2);
     }
     // final state: thread v holds column v of S; a warp's store of row k covers 128 contiguous bytes
