@@ -1,23 +1,25 @@
 // a1, tensor-core path.  Chunked gated delta rule (chunk 64, dk = dv = 128, bf16 activations,
 // fp32 state) on the 5th-generation tensor cores of sm_100a.
 //
-// One CTA (two warpgroups) per (sequence, value head); the fp32 state S [dk][dv] lives in TMEM for
-// the whole sequence.  The chunk algebra of fast_chunk_gated_delta_rule_v2
-// (src/gdn_chunk_fast2.py:37-59) is split into the part that does not depend on S and the part
-// that does, and the two run as a software pipeline on separate warpgroups:
+// Persistent CTAs (one per SM, three warpgroups) walk a list of (sequence, value head) items; the
+// fp32 state lives in TMEM, transposed (S^T: lane v, column k), for the whole item.  The chunk
+// algebra of fast_chunk_gated_delta_rule_v2 (src/gdn_chunk_fast2.py:37-59) is split into the part
+// that does not depend on S and the part that does, and the two run as a software pipeline:
 //
-//   intra-chunk warpgroup (warps 0-3), chunk j:
+//   intra-chunk group (warps 0-7), chunk j:
 //       TMA loads of raw q, k (un-repeated k-head) and v tiles (128-byte swizzle; never multicast)
 //       P1  [Q;K] [Q;K]^T  -> QK^T, KK^T and, on the diagonal, the squared row norms that give the
 //                             l2-norm factors rq, rk (rounded in bf16 as src/gdn_chunk_fast.py:17-18)
 //       CUDA cores: X = -(beta k k^T . decay) strictly lower; T = (I - X)^-1 by the blocked
 //                   inverse of src/gdn_chunk_fast.py:21-62; QKm = (q k^T . decay) causal
 //       P2  U^T = V^T (T diag beta)^T          P3  W^T = K^T (T diag(beta e^gc rk))^T
-//   recurrence warpgroup (warps 4-7), chunk j-1 (or j once the intra group hands it over):
+//   recurrence group (warps 8-11), chunk j-1 (or j once the intra group hands it over):
 //       P4  vn^T = U^T - S^T W^T                (a-negated accumulate onto U^T)
 //       P5  o^T  = (S^T Q^T) . (rq scale e^gc) + vn^T QKm^T    (two accumulators)
-//       P6  S    = S e^gl + K^T (vn . rk e^(gl-gc))            (S pre-scaled when read)
-//       output through shared memory (a TMA store for full chunks), final S to the slot's pool row
+//       P6  S^T  = S^T e^gl + (vn . rk e^(gl-gc))^T K         (S pre-scaled when read)
+//       S^T, vn^T and (vn . rk e^(gl-gc))^T are the A operands of P4-P6, taken from bf16 copies in
+//       TMEM; the output leaves through a swizzled shared tile (TMA stores for full chunks) and the
+//       final state goes to the slot's pool row.
 //
 // Hand-over uses mbarriers ("chunk ready" / "buffers freed"); per-chunk TMEM accumulators, the QKm
 // tile and the per-chunk vectors are double buffered so the intra group can run a chunk ahead.
@@ -706,7 +708,7 @@ __global__ void __launch_bounds__(kNT, 1)
       if (rt == 0) bulk_wait_read();  // the previous chunk's output store has left W_WT
       group_sync(2);
       const int nt = cv.nt;
-      {  // S -> bf16 tile (operand of P4/P5), S e^gl -> TMEM (P6 accumulates onto it); W^T tile
+      {  // S^T -> bf16 copy in TMEM (A of P4/P5), S^T e^gl back into TMEM (P6 accumulates onto it); W^T tile
         const float Gl = cv.Gl;
 #pragma unroll
         for (int part = 0; part < 4; ++part) {
@@ -741,7 +743,7 @@ __global__ void __launch_bounds__(kNT, 1)
       if (ok && !mbar_wait(bar_mr, ph_mr)) ok = false;
       ph_mr ^= 1u;
       tc_fence_after();
-      {  // vn^T tiles: plain (P5) and scaled by rk e^(gl-gc) (P6)
+      {  // vn^T as bf16 copies in TMEM: plain (A of vn^T QKm^T) and scaled by rk e^(gl-gc) (A of P6)
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
           float a[32], d[32];
