@@ -137,3 +137,38 @@ def test_bf16_rounding_known_values():
     assert u[0] == 0x3F80 and u[1] == 0x3F80          # 1 + 2^-8 is a tie -> even (1.0)
     assert u[2] == 0x3F81                              # above the tie -> rounds up
     assert np.array_equal(O.from_bf16_bits(u), O.bf16(x))
+
+
+def test_empty_sequences_are_the_zero_chunk_limit():
+    """Packed prefill with empty sequences (the library's definition; the reference's chunk function
+    raises on L = 0): no output rows, final state = initial state or zeros, and the other sequences
+    unchanged by the empty ones around them; the prefill conv keeps the carried window or zeros."""
+    rng = np.random.default_rng(31)
+    Hk, Hv, d = 1, 2, 64
+    lens_a, lens_b = [0, 70, 0, 5, 0], [70, 5]
+    Tt = sum(lens_a)
+    q = rng.standard_normal((Tt, Hk, d)).astype(np.float32)
+    k = rng.standard_normal((Tt, Hk, d)).astype(np.float32)
+    v = rng.standard_normal((Tt, Hv, d)).astype(np.float32)
+    g = -rng.uniform(0.01, 1, (Tt, Hv)).astype(np.float32)
+    be = rng.uniform(0, 1, (Tt, Hv)).astype(np.float32)
+    pool0 = (0.1 * rng.standard_normal((6, Hv, d, d))).astype(np.float32)
+    cu_a = np.concatenate([[0], np.cumsum(lens_a)]).astype(np.int32)
+    cu_b = np.concatenate([[0], np.cumsum(lens_b)]).astype(np.int32)
+    pa, pb = pool0.copy(), pool0.copy()
+    oa, _ = O.prefill_varlen(q, k, v, g, be, cu_a, pa, np.array([1, 2, 3, 4, 5]), np.array([1, 1, 0, 1, 0]), True, "f32")
+    ob, _ = O.prefill_varlen(q, k, v, g, be, cu_b, pb, np.array([2, 4]), np.array([1, 1]), True, "f32")
+    assert oa.shape == (Tt, Hv, d) and np.array_equal(oa, ob)
+    assert np.array_equal(pa[2], pb[2]) and np.array_equal(pa[4], pb[4])
+    assert np.array_equal(pa[1], pool0[1])           # empty, from its initial state
+    assert not pa[3].any() and not pa[5].any()       # empty, from zeros
+    # conv: an empty sequence keeps its window (carried) or gets zeros
+    C, K = 8, 4
+    x = rng.standard_normal((Tt, C)).astype(np.float32)
+    w = rng.uniform(-0.5, 0.5, (C, K)).astype(np.float32)
+    init = rng.standard_normal((len(lens_a), C, K)).astype(np.float32)
+    y, st = O.prefill_conv(x, cu_a, w, None, init, "f32")
+    assert np.array_equal(st[0], init[0]) and np.array_equal(st[2], init[2])
+    y0, st0 = O.prefill_conv(x, cu_a, w, None, None, "f32")
+    assert not st0[0].any() and not st0[4].any()
+
