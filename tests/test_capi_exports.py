@@ -102,3 +102,45 @@ def test_ops_refuse_cpu_tensors():
     x = torch.zeros(4, 128, dtype=torch.bfloat16)
     with pytest.raises(RuntimeError, match="CUDA"):
         ops.gated_rmsnorm(x, x, torch.ones(128, dtype=torch.bfloat16))
+
+
+def test_header_compiles_as_c_and_links(tmp_path):
+    """A C caller (no Python, no torch) includes include/gdn_b200.h, links libgdn_b200.so and gets the
+    library's status codes and messages: the boundary is a plain C ABI.  Only argument validation runs
+    (no CUDA call), so no GPU is needed."""
+    import shutil
+    import subprocess
+    gcc = shutil.which("gcc")
+    if gcc is None:
+        pytest.skip("gcc not available")
+    L = pkg("_lib")
+    if not os.path.exists(L.LIB_PATH):
+        pytest.fail("libgdn_b200.so is not built (run __graft_entry__.build())")
+    src = tmp_path / "caller.c"
+    src.write_text(r'''
+#include <stdio.h>
+#include <string.h>
+#include "gdn_b200.h"
+int main(void) {
+  if (gdn_version() < 100) return 1;
+  /* one sequence of 10 tokens with every tensor pointer missing: rejected before any CUDA call */
+  int rc = gdn_chunk_prefill(NULL, 0, NULL, 0, NULL, 0, NULL, NULL, 0, NULL, 1, 10, NULL, NULL, NULL, NULL,
+                             NULL, 0, NULL, 0, 16, 48, 128, 128, 1, GDN_BF16, NULL, NULL);
+  if (rc != GDN_ERR_ARG || strstr(gdn_last_error(), "null") == NULL) return 2;
+  /* a head ratio the library does not build (40 value heads over 16 key heads); cu_seqlens is a device
+     pointer the host never dereferences, so any non-null value reaches the shape check */
+  const int32_t* cu = (const int32_t*)(uintptr_t)4096;
+  rc = gdn_chunk_prefill_gates(NULL, 0, NULL, 0, NULL, 0, NULL, NULL, 0, NULL, NULL, cu, 1, 0, NULL, NULL, NULL,
+                               NULL, NULL, 0, NULL, 0, 16, 40, 128, 128, 1, GDN_BF16, NULL, NULL);
+  if (rc != GDN_ERR_SHAPE || strstr(gdn_last_error(), "multiple") == NULL) return 3;
+  printf("ok %d\n", gdn_version());
+  return 0;
+}
+''')
+    exe = tmp_path / "caller"
+    libdir = os.path.dirname(L.LIB_PATH)
+    r = subprocess.run([gcc, "-std=c99", "-Wall", "-Werror", "-I", os.path.join(ROOT, "include"), str(src), "-o",
+                        str(exe), "-L", libdir, "-lgdn_b200", f"-Wl,-rpath,{libdir}"], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0 and r.stdout.startswith("ok"), (r.returncode, r.stdout, r.stderr)
