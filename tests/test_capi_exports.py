@@ -102,6 +102,11 @@ def test_ops_refuse_cpu_tensors():
     x = torch.zeros(4, 128, dtype=torch.bfloat16)
     with pytest.raises(RuntimeError, match="CUDA"):
         ops.gated_rmsnorm(x, x, torch.ones(128, dtype=torch.bfloat16))
+    q = torch.zeros(4, 1, 128, dtype=torch.bfloat16)
+    ab = torch.zeros(4, 3, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        ops.chunk_prefill_varlen_gates(q, q, torch.zeros(4, 3, 128, dtype=torch.bfloat16), ab, ab, torch.zeros(3),
+                                       torch.zeros(3), torch.tensor([0, 4], dtype=torch.int32))
 
 
 def test_header_compiles_as_c_and_links(tmp_path):
