@@ -10,13 +10,19 @@
 // from a fixed-size array in device memory that belongs to the library instead.
 //
 // The array (kNoAllocScratchBytes) lives in every GPU that loads the library until the process
-// exits.  Its device address is looked up once per device, on the first call made with that
-// device current; make that first call before any stream capture.  All calls on a device share
-// the one array and it keeps whatever the last call left there.  The counters must start at
-// zero: a static device array is zero when the library loads, and every call returns each counter
-// it used to zero, so no clearing is needed between calls (the prepared rows need no clearing).
-// Two calls whose kernels overlap on the GPU (different streams, no ordering between them) race
-// on the array.  Requests larger than the array are rejected with GDN_ERR_WORKSPACE; nothing here
+// exits.  It has two parts that never overlap:
+//   * bytes [0, kPrepBytes): the prepared rows and gates of dk = dv = 128 calls.  Every call
+//     writes them before it reads them, so what an earlier call left there does not matter.
+//   * bytes [kPrepBytes, kNoAllocScratchBytes): the ticket counters of dk = dv = 64 calls.  They
+//     must be zero when a call starts.  The array is zero when the library loads, no dk = 128
+//     call writes this part, and every dk = 64 call that runs to its end returns each counter it
+//     used to zero (a call stopped by a bad slot index takes no ticket).
+// Its device address is looked up once per device, on the first call made with that device
+// current; make that first call before any stream capture.  The cached address belongs to the
+// device's primary context: do not use this entry point across a cudaDeviceReset of that device.
+// All calls on a device share the one array and it keeps whatever the last call left there.  Two
+// calls whose kernels overlap on the GPU (different streams, no ordering between them) race on
+// the array.  Requests larger than their part are rejected with GDN_ERR_WORKSPACE; nothing here
 // calls cudaMalloc, cudaFree or any allocating library routine.
 #include <mutex>
 
@@ -25,6 +31,9 @@
 namespace gdn {
 
 constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;  // 8 MiB per GPU
+constexpr size_t kTicketBytes = size_t(256) << 10;          // dk = dv = 64 counters (the tail)
+constexpr size_t kPrepBytes = kNoAllocScratchBytes - kTicketBytes;  // dk = dv = 128 rows and gates
+static_assert(kPrepBytes % 256 == 0, "the ticket part keeps the array's 256-byte alignment");
 constexpr int kMaxDevices = 64;
 
 static __device__ __align__(256) unsigned char g_decode_scratch[kNoAllocScratchBytes];
@@ -52,7 +61,9 @@ static int scratch_address(void** out) {
 
 }  // namespace gdn
 
-extern "C" size_t gdn_decode_layer_noalloc_max_bytes(void) { return gdn::kNoAllocScratchBytes; }
+extern "C" size_t gdn_decode_layer_noalloc_max_bytes(void) { return gdn::kPrepBytes; }
+
+extern "C" size_t gdn_decode_layer_noalloc_max_ticket_bytes(void) { return gdn::kTicketBytes; }
 
 extern "C" int gdn_decode_layer_noalloc(const void* mixed_qkv, int64_t mixed_rs, const void* z, const void* a,
                                         const void* b, const float* A_log, const float* dt_bias,
@@ -64,15 +75,17 @@ extern "C" int gdn_decode_layer_noalloc(const void* mixed_qkv, int64_t mixed_rs,
   if (n < 0 || Hk <= 0 || Hv <= 0 || dk <= 0 || dv <= 0)
     return fail(GDN_ERR_ARG, "gdn_decode_layer_noalloc: n=%d Hk=%d Hv=%d dk=%d dv=%d", n, Hk, Hv, dk, dv);
   const size_t need = gdn_decode_layer_workspace_size(n, Hk, Hv, dk, dv, dtype);
-  if (need > kNoAllocScratchBytes)
+  const bool wide = dk == 128 && dv == 128;  // prepared rows (else ticket counters)
+  const size_t cap = wide ? kPrepBytes : kTicketBytes;
+  if (need > cap)
     return fail(GDN_ERR_WORKSPACE,
-                "gdn_decode_layer_noalloc: needs %zu bytes of scratch, the built-in array holds %zu "
-                "(gdn_decode_layer_workspace_size bytes must fit)",
-                need, kNoAllocScratchBytes);
+                "gdn_decode_layer_noalloc: needs %zu bytes of scratch, the built-in array's %s part holds %zu",
+                need, wide ? "prepared-row" : "ticket", cap);
   void* scratch = nullptr;
   int rc = scratch_address(&scratch);
   if (rc) return rc;
+  void* ws = wide ? scratch : static_cast<void*>(static_cast<unsigned char*>(scratch) + kPrepBytes);
   return gdn_decode_layer(mixed_qkv, mixed_rs, z, a, b, A_log, dt_bias, conv_w, conv_b, conv_pool, rec_pool,
-                          slot_idx, n_slots, norm_w, eps, out, n, Hk, Hv, dk, dv, K, conv_mode, scratch,
-                          kNoAllocScratchBytes, dtype, err_flag, stream);
+                          slot_idx, n_slots, norm_w, eps, out, n, Hk, Hv, dk, dv, K, conv_mode, ws, cap, dtype,
+                          err_flag, stream);
 }

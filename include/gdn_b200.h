@@ -163,16 +163,21 @@ GDN_API int gdn_decode_layer(const void* mixed_qkv, int64_t mixed_rs, const void
  * separates workspace from its torch ops.  Hosts such as a serving runtime
  * that owns the whole device-memory budget, or a decode loop that cannot pay
  * cudaMalloc's implicit synchronisation, pass only inputs and outputs here; the
- * workspace is a fixed array of gdn_decode_layer_noalloc_max_bytes() (8 MiB)
- * inside the library, held by every GPU that loads it until exit.  Its address
+ * workspace is a fixed 8 MiB array inside the library, held by every GPU that
+ * loads it until exit.  The array has two parts that never overlap:
+ * gdn_decode_layer_noalloc_max_bytes() bytes for the prepared rows and gates
+ * of dk = dv = 128 calls (written before they are read), and
+ * gdn_decode_layer_noalloc_max_ticket_bytes() bytes for the ticket counters of
+ * dk = dv = 64 calls (zero when the library loads; every call that runs to
+ * its end leaves them zero, and no dk = 128 call touches them).  Its address
  * is looked up on the first call per device (make that call before any stream
- * capture).  All calls on a device share that array: calls whose kernels
- * overlap on the GPU race.  It holds the workspace described above (the
- * tickets are zero when the library loads, and every call leaves them zero).
- * Requests larger than the array return
- * GDN_ERR_WORKSPACE.  Arguments as gdn_decode_layer minus the workspace.
+ * capture; do not use the entry point across a cudaDeviceReset).  All calls on
+ * a device share that array: calls whose kernels overlap on the GPU race.
+ * Requests larger than their part return GDN_ERR_WORKSPACE.  Arguments as
+ * gdn_decode_layer minus the workspace.
  */
 GDN_API size_t gdn_decode_layer_noalloc_max_bytes(void);
+GDN_API size_t gdn_decode_layer_noalloc_max_ticket_bytes(void);
 
 GDN_API int gdn_decode_layer_noalloc(const void* mixed_qkv, int64_t mixed_rs, const void* z, const void* a,
                                      const void* b, const float* A_log, const float* dt_bias,
