@@ -87,6 +87,10 @@ class CBEngine:
         self._tok = torch.zeros(n_slots, dtype=torch.long, device=self.dev)
         self._pos = torch.zeros(n_slots, dtype=torch.long, device=self.dev)
         self._slot = torch.arange(n_slots, dtype=torch.int32, device=self.dev)
+        # Device error flag shared by every kernel call of the engine (0 = fine, 1 = a slot index
+        # outside the pools, 2 = a bounded wait inside a kernel ran out).  It is read back with the
+        # tokens each step already copies to the host, so checking it costs no extra sync.
+        self._err = torch.zeros(1, dtype=torch.int32, device=self.dev)
         self.graph_decode = graph_decode
         self._graphs, self._graph_out = {}, {}
         if graph_decode:
@@ -124,6 +128,7 @@ class CBEngine:
         for d in (self.kv_k, self.kv_v, self.conv, self.rec):
             for t in d.values():
                 t.zero_()
+        self._err.zero_()
         self.lens = [0] * self.N
 
     # ------------------------------------------------------------------ decode
@@ -142,7 +147,7 @@ class CBEngine:
         v = at.v_proj(h).view(n, 1, kvh, hd).transpose(1, 2)
         q, k = self.M.apply_rotary_pos_emb(q, k, cos, sin)
         o = ops.attn_decode(q[:, :, 0], k[:, :, 0], v[:, :, 0], self.kv_k[i], self.kv_v[i], self._slot, pos32, Lmax,
-                            at.scaling, gate=gate, workspace=self._attn_ws)
+                            at.scaling, gate=gate, workspace=self._attn_ws, err=self._err)
         return at.o_proj(o.reshape(n, 1, -1))
 
     def _gdn(self, gd, i, h):
@@ -154,7 +159,8 @@ class CBEngine:
         a = gd.in_proj_a(h).reshape(n, -1)
         core = ops.decode_layer(mixed, z, a, b, p["A_log"], p["dt_bias"], p["conv_w"], p["conv_b"], self.conv[i],
                                 self.rec[i], self._slot, p["norm_w"], p["eps"], p["Hk"], p["Hv"], p["dk"], p["dv"],
-                                ops.GDN_CONV_ELEM if ELEM_CONV else ops.GDN_CONV_HF, workspace=self._ws)
+                                ops.GDN_CONV_ELEM if ELEM_CONV else ops.GDN_CONV_HF, workspace=self._ws,
+                                err=self._err)
         return gd.out_proj(core.reshape(n, 1, -1))
 
     def _core(self, Lmax):
@@ -173,7 +179,26 @@ class CBEngine:
             x = x + h
             x = x + layer.mlp(layer.post_attention_layernorm(x))
         x = self.lm.norm(x)
-        return self.model.lm_head(x[:, 0]).argmax(-1)
+        # next tokens and, as the last entry, the error flag after this step's kernels
+        return torch.cat([self._greedy(x[:, 0]), self._err.to(torch.long)])
+
+    def _greedy(self, h):
+        """Greedy next token per row of the final hidden states (a vocabulary-parallel head
+        provides its own cross-rank argmax)."""
+        head = self.model.lm_head
+        pick = getattr(head, "greedy", None)
+        return pick(h) if pick is not None else head(h).argmax(-1)
+
+    _ERRORS = {1: "a slot index outside the state pools", 2: "a bounded wait inside a kernel ran out"}
+
+    def _raise_on(self, code, what):
+        if code:
+            self._err.zero_()
+            raise RuntimeError(f"{what}: device error {code} ({self._ERRORS.get(code, 'unknown')})")
+
+    def check_errors(self):
+        """Raise RuntimeError if a kernel of this engine reported an error since the last check."""
+        self._raise_on(int(self._err.item()), "CBEngine")
 
     @torch.inference_mode()
     def decode_step(self, slots, tokens, hold=()):
@@ -199,6 +224,7 @@ class CBEngine:
             nxt = self._graph_out[b].tolist()
         else:
             nxt = self._core(L).tolist()
+        self._raise_on(nxt[N], "decode_step")
         for s in slots:
             self.lens[s] += 1
         return [nxt[s] for s in slots]
@@ -243,13 +269,14 @@ class CBEngine:
         z = gd.in_proj_z(h)[0].reshape(T, Hv, dv)
         b = gd.in_proj_b(h)[0]
         a = gd.in_proj_a(h)[0]
-        y = ops.prefill_conv_varlen(mixed, cu_d, p["conv_w"], p["conv_b"], self.conv[i], slot_t, use_init)
+        y = ops.prefill_conv_varlen(mixed, cu_d, p["conv_w"], p["conv_b"], self.conv[i], slot_t, use_init,
+                                    err=self._err)
         q = y[:, :Hk * dk].view(T, Hk, dk)
         k = y[:, Hk * dk:2 * Hk * dk].view(T, Hk, dk)
         v = y[:, 2 * Hk * dk:].view(T, Hv, dv)
         # beta = sigmoid(b) and g = -exp(A_log) softplus(a + dt_bias) are formed inside the kernel
         core = ops.chunk_prefill_varlen_gates(q, k, v, a, b, p["A_log"], p["dt_bias"], cu_d, self.rec[i], slot_t,
-                                              use_init, True)
+                                              use_init, True, err=self._err)
         core = ops.gated_rmsnorm(core, z, p["norm_w"], p["eps"])
         return gd.out_proj(core.reshape(1, T, -1))
 
@@ -285,7 +312,9 @@ class CBEngine:
             x = x + layer.mlp(layer.post_attention_layernorm(x))
         last = torch.tensor([c - 1 for c in cu[1:]], dtype=torch.long, device=self.dev)
         xl = self.lm.norm(x[0, last])
-        firsts = self.model.lm_head(xl).argmax(-1).tolist()
+        res = torch.cat([self._greedy(xl), self._err.to(torch.long)]).tolist()
+        self._raise_on(res[-1], "prefill_batch")
+        firsts = res[:-1]
         for slot, st, L in zip(slots, starts, lens):
             self.lens[slot] = st + L
         return firsts

@@ -5,7 +5,8 @@ Mirrors the reference's src/cb_tp.py:
     ranks; the engine's attention ``o_proj``, GDN ``out_proj`` and MLP ``down_proj`` become this.
   * ``shard_model`` (src/cb_tp.py:47-106): per rank, a contiguous block of attention q heads, GDN
     k heads (with their q/k conv channels) and v heads (with their v conv channels, a/b/A_log/
-    dt_bias rows, z rows and out_proj columns), and a block of MLP columns.
+    dt_bias rows, z rows and out_proj columns), and a block of MLP columns, applied from one
+    table of (weight, axis, index) cuts; optionally the LM head split by vocabulary.
   * ``TPEngine`` (src/cb_tp.py:117-285): the engine on sharded weights.
   * ``PeerAllReduce``: the sum over ranks for decode-sized outputs by this library's own kernel over
     IPC-mapped peer buffers (gdn_allreduce); NCCL keeps the larger (prefill) ones.
@@ -119,30 +120,51 @@ def disable_peer_allreduce():
 
 
 class AllReduceLinear(nn.Module):
-    """Row-parallel linear: local partial product, then the sum over ranks (identical on all):
-    the peer-memory kernel for decode-sized outputs when enabled, NCCL otherwise."""
+    """A row-parallel projection: this rank holds a block of the input columns, so its product is
+    a partial sum; the full output is the sum of the partials over all ranks (the same on every
+    rank afterwards).  Decode-sized outputs are summed by the peer-memory kernel when one is
+    enabled, everything else by NCCL (src/cb_tp.py:25-35 is the reference's version)."""
 
     def __init__(self, lin):
         super().__init__()
         self.lin = lin
 
     def forward(self, x):
-        y = self.lin(x)
-        ar = _PEER_AR
-        if ar is not None and ar.applies(y):
-            ar(y)
+        partial = self.lin(x)
+        reducer = _PEER_AR
+        if reducer is None or not reducer.applies(partial):
+            dist.all_reduce(partial)
         else:
-            dist.all_reduce(y)
-        return y
+            reducer(partial)
+        return partial
 
 
-def _set_weight(lin, w):
-    lin.weight = nn.Parameter(w.contiguous(), requires_grad=False)
-    lin.out_features, lin.in_features = w.shape[0], w.shape[1]
+class VocabParallelHead(nn.Module):
+    """The LM head split by vocabulary: this rank keeps rows [v0, v0 + V/tp) of the full weight
+    and returns their logits.  ``greedy`` gives the full-vocabulary argmax with one all-reduce of
+    8 bytes per row: each rank packs (its best logit, its best global id) into an int64 whose
+    signed order is (logit ascending, id descending), and the MAX over ranks is the winner, the
+    lowest id among equal logits, as torch.argmax over the full row picks.  Not in the reference
+    (its TP engine keeps the whole head on every rank, src/cb_tp.py:117-285)."""
 
+    def __init__(self, lin, v0):
+        super().__init__()
+        self.lin = lin
+        self.v0 = int(v0)
 
-def _rows(start, count, device):
-    return torch.arange(start, start + count, device=device)
+    def forward(self, x):
+        return self.lin(x)
+
+    def greedy(self, x):
+        logits = self.lin(x).float()
+        best, arg = logits.max(dim=-1)
+        bits = best.contiguous().view(torch.int32).to(torch.int64)
+        # IEEE order as a signed integer: negative floats have their magnitude bits flipped
+        key = torch.where(bits < 0, bits ^ 0x7FFFFFFF, bits)
+        gid = arg.to(torch.int64) + self.v0
+        packed = (key << 32) | (0xFFFFFFFF - gid)
+        dist.all_reduce(packed, op=dist.ReduceOp.MAX)
+        return 0xFFFFFFFF - (packed & 0xFFFFFFFF)
 
 
 def attention_head_split(nh, kvh, tp, rank):
@@ -167,65 +189,126 @@ def attention_head_split(nh, kvh, tp, rank):
     return q0, nh_l, kv, 1
 
 
-def shard_model(model, rank, tp):
-    """In-place sharding of a freshly loaded Qwen3_5ForConditionalGeneration (src/cb_tp.py:47-106)."""
+def _span(first, count, width, base=0):
+    """Indices of ``count`` consecutive blocks of ``width`` starting at block ``first``."""
+    return torch.arange(base + first * width, base + (first + count) * width)
+
+
+class ShardPlan:
+    """Which output rows / input columns of each weight one rank keeps, as index tensors.
+
+    The layouts are fixed by the checkpoint: q_proj holds, per attention head, its query rows
+    followed by its gate rows; in_proj_qkv and the GDN conv hold the channels [q | k | v] with q
+    and k by k-head and v by v-head; in_proj_z and out_proj hold v-head blocks of dv; in_proj_a /
+    in_proj_b / A_log / dt_bias one entry per v-head; the MLP one entry per hidden unit.  A rank
+    takes one contiguous block of heads (or units) of each kind."""
+
+    def __init__(self, cfg, rank, tp):
+        hd = cfg.head_dim
+        nh, kvh = cfg.num_attention_heads, cfg.num_key_value_heads
+        self.q0, self.nq, self.kv0, self.nkv = attention_head_split(nh, kvh, tp, rank)
+        kh, vh = cfg.linear_num_key_heads, cfg.linear_num_value_heads
+        dk, dv = cfg.linear_key_head_dim, cfg.linear_value_head_dim
+        if kh % tp or vh % tp:
+            raise ValueError(f"GDN heads ({kh} k, {vh} v) do not split over tp={tp}")
+        self.nkh, self.nvh = kh // tp, vh // tp
+        ffn = cfg.intermediate_size
+        if ffn % tp:
+            raise ValueError(f"MLP width {ffn} does not split over tp={tp}")
+        k_first, v_first = rank * self.nkh, rank * self.nvh
+        self.index = {
+            "attn_qg": _span(self.q0, self.nq, 2 * hd),
+            "attn_kv": _span(self.kv0, self.nkv, hd),
+            "attn_o": _span(self.q0, self.nq, hd),
+            "gdn_qkv": torch.cat([_span(k_first, self.nkh, dk), _span(k_first, self.nkh, dk, kh * dk),
+                                  _span(v_first, self.nvh, dv, 2 * kh * dk)]),
+            "gdn_v": _span(v_first, self.nvh, dv),
+            "gdn_heads": _span(v_first, self.nvh, 1),
+            "ffn": _span(rank, 1, ffn // tp),
+        }
+
+
+# (layer type or "*", path inside the decoder layer, axis kept, plan index, row-parallel).  Axis 0
+# keeps output rows (the module's input stays whole); axis 1 keeps input columns, which makes the
+# product a partial sum that AllReduceLinear completes.
+_CUTS = (
+    ("full_attention", "self_attn.q_proj", 0, "attn_qg", False),
+    ("full_attention", "self_attn.k_proj", 0, "attn_kv", False),
+    ("full_attention", "self_attn.v_proj", 0, "attn_kv", False),
+    ("full_attention", "self_attn.o_proj", 1, "attn_o", True),
+    ("linear_attention", "linear_attn.in_proj_qkv", 0, "gdn_qkv", False),
+    ("linear_attention", "linear_attn.conv1d", 0, "gdn_qkv", False),
+    ("linear_attention", "linear_attn.in_proj_z", 0, "gdn_v", False),
+    ("linear_attention", "linear_attn.in_proj_b", 0, "gdn_heads", False),
+    ("linear_attention", "linear_attn.in_proj_a", 0, "gdn_heads", False),
+    ("linear_attention", "linear_attn.A_log", 0, "gdn_heads", False),
+    ("linear_attention", "linear_attn.dt_bias", 0, "gdn_heads", False),
+    ("linear_attention", "linear_attn.out_proj", 1, "gdn_v", True),
+    ("*", "mlp.gate_proj", 0, "ffn", False),
+    ("*", "mlp.up_proj", 0, "ffn", False),
+    ("*", "mlp.down_proj", 1, "ffn", True),
+)
+
+
+def _keep(t, axis, idx):
+    return nn.Parameter(t.detach().index_select(axis, idx.to(t.device)).contiguous(), requires_grad=False)
+
+
+def _cut(layer, path, axis, idx, row_parallel):
+    parent_path, _, name = path.rpartition(".")
+    parent = layer.get_submodule(parent_path)
+    obj = getattr(parent, name)
+    if isinstance(obj, nn.Parameter):            # a per-head vector
+        setattr(parent, name, _keep(obj, axis, idx))
+        return
+    obj.weight = _keep(obj.weight, axis, idx)
+    if obj.bias is not None and axis == 0:       # a row-parallel bias would be summed tp times
+        obj.bias = _keep(obj.bias, 0, idx)
+    elif obj.bias is not None:
+        raise ValueError(f"{path}: a bias on a row-parallel projection is not supported")
+    n = idx.numel()
+    if isinstance(obj, nn.Linear):
+        if axis == 0:
+            obj.out_features = n
+        else:
+            obj.in_features = n
+    elif isinstance(obj, nn.Conv1d):             # depthwise: channels and groups follow the rows
+        obj.in_channels = obj.out_channels = obj.groups = n
+    if row_parallel:
+        setattr(parent, name, AllReduceLinear(obj))
+
+
+def shard_model(model, rank, tp, vocab_parallel=False):
+    """Shard a freshly built Qwen3_5ForConditionalGeneration in place for ``rank`` of ``tp`` (the
+    layout of src/cb_tp.py:47-106, with KV heads replicated when tp > kv heads).  With
+    ``vocab_parallel`` the LM head keeps V / tp rows per rank (VocabParallelHead)."""
     cfg = model.config.text_config
-    assert tp > 0 and rank < tp
-    assert not getattr(cfg, "attention_bias", False), "attention_bias not supported in TP"
-    hd = cfg.head_dim
-    nh, kvh = cfg.num_attention_heads, cfg.num_key_value_heads
+    if not 0 <= rank < tp:
+        raise ValueError(f"rank {rank} outside tp={tp}")
+    if getattr(cfg, "attention_bias", False):
+        raise ValueError("attention_bias is not supported under TP")
+    plan = ShardPlan(cfg, rank, tp)
     lm = model.model.language_model
-    H = cfg.hidden_size
-    q0, nh_l, kv0, kvh_l = attention_head_split(nh, kvh, tp, rank)
-    for i, layer in enumerate(lm.layers):
-        if cfg.layer_types[i] == "full_attention":
-            at = layer.self_attn
-            # q_proj: per head [q(hd), gate(hd)] interleaved; a contiguous block of heads
-            _set_weight(at.q_proj, at.q_proj.weight.view(nh, 2 * hd, H)[q0:q0 + nh_l].reshape(-1, H))
-            _set_weight(at.k_proj, at.k_proj.weight[kv0 * hd:(kv0 + kvh_l) * hd])
-            _set_weight(at.v_proj, at.v_proj.weight[kv0 * hd:(kv0 + kvh_l) * hd])
-            _set_weight(at.o_proj, at.o_proj.weight.view(H, nh, hd)[:, q0:q0 + nh_l].reshape(H, -1))
-            at.o_proj = AllReduceLinear(at.o_proj)
-            at.num_key_value_groups = nh_l // kvh_l
+    for kind, layer in zip(cfg.layer_types, lm.layers):
+        for want, path, axis, key, row_parallel in _CUTS:
+            if want in ("*", kind):
+                _cut(layer, path, axis, plan.index[key], row_parallel)
+        if kind == "full_attention":
+            layer.self_attn.num_key_value_groups = plan.nq // plan.nkv
         else:
             gd = layer.linear_attn
-            kh, vh = gd.num_k_heads, gd.num_v_heads
-            dk, dv = gd.head_k_dim, gd.head_v_dim
-            if kh % tp or vh % tp:
-                raise ValueError(f"GDN heads ({kh} k, {vh} v) do not split over tp={tp}")
-            kh_l, vh_l = kh // tp, vh // tp
-            key_dim = gd.key_dim
-            # in_proj_qkv rows: [q (kh*dk) | k (kh*dk) | v (vh*dv)]; the same head blocks in each part
-            dev = gd.in_proj_qkv.weight.device
-            idx = torch.cat([_rows(rank * kh_l * dk, kh_l * dk, dev), _rows(key_dim + rank * kh_l * dk, kh_l * dk, dev),
-                             _rows(2 * key_dim + rank * vh_l * dv, vh_l * dv, dev)])
-            _set_weight(gd.in_proj_qkv, gd.in_proj_qkv.weight.index_select(0, idx))
-            gd.conv1d.weight = nn.Parameter(gd.conv1d.weight.index_select(0, idx).contiguous(), requires_grad=False)
-            if gd.conv1d.bias is not None:
-                gd.conv1d.bias = nn.Parameter(gd.conv1d.bias.index_select(0, idx).contiguous(), requires_grad=False)
-            gd.conv1d.out_channels = gd.conv1d.in_channels = idx.numel()
-            gd.conv1d.groups = idx.numel()
-            vrows = _rows(rank * vh_l * dv, vh_l * dv, dev)
-            _set_weight(gd.in_proj_z, gd.in_proj_z.weight.index_select(0, vrows))
-            hrows = _rows(rank * vh_l, vh_l, dev)
-            _set_weight(gd.in_proj_b, gd.in_proj_b.weight.index_select(0, hrows))
-            _set_weight(gd.in_proj_a, gd.in_proj_a.weight.index_select(0, hrows))
-            gd.A_log = nn.Parameter(gd.A_log.data[hrows].contiguous(), requires_grad=False)
-            gd.dt_bias = nn.Parameter(gd.dt_bias.data[hrows].contiguous(), requires_grad=False)
-            _set_weight(gd.out_proj, gd.out_proj.weight[:, rank * vh_l * dv:(rank + 1) * vh_l * dv])
-            gd.out_proj = AllReduceLinear(gd.out_proj)
-            gd.num_k_heads, gd.num_v_heads = kh_l, vh_l
-            gd.key_dim, gd.value_dim = kh_l * dk, vh_l * dv
+            gd.num_k_heads, gd.num_v_heads = plan.nkh, plan.nvh
+            gd.key_dim, gd.value_dim = plan.nkh * gd.head_k_dim, plan.nvh * gd.head_v_dim
             gd.conv_dim = 2 * gd.key_dim + gd.value_dim
-        mlp = layer.mlp
-        inter = mlp.gate_proj.weight.shape[0]
-        if inter % tp:
-            raise ValueError(f"MLP width {inter} does not split over tp={tp}")
-        r0, r1 = rank * (inter // tp), (rank + 1) * (inter // tp)
-        _set_weight(mlp.gate_proj, mlp.gate_proj.weight[r0:r1])
-        _set_weight(mlp.up_proj, mlp.up_proj.weight[r0:r1])
-        _set_weight(mlp.down_proj, mlp.down_proj.weight[:, r0:r1])
-        mlp.down_proj = AllReduceLinear(mlp.down_proj)
+    if vocab_parallel and tp > 1:
+        V = model.lm_head.weight.shape[0]
+        if V % tp:
+            raise ValueError(f"vocabulary {V} does not split over tp={tp}")
+        rows = _span(rank, 1, V // tp)
+        head = model.lm_head
+        head.weight = _keep(head.weight, 0, rows)
+        head.out_features = V // tp
+        model.lm_head = VocabParallelHead(head, rank * (V // tp))
     return model
 
 
@@ -257,7 +340,9 @@ class TPEngine(CBEngine):
         super().__init__(model, n_slots, t_max, device, graph_decode=graph_decode, tp=tp)
 
     def check_errors(self):
-        """Raise if a peer all-reduce timed out (a rank did not arrive)."""
+        """Raise if a kernel of the engine reported an error or a peer all-reduce timed out (a rank
+        did not arrive)."""
+        super().check_errors()
         if self.peer_ar is not None and int(self.peer_ar.err.item()) != 0:
             raise RuntimeError(f"peer all-reduce error {int(self.peer_ar.err.item())} (a rank did not arrive)")
 

@@ -13,10 +13,11 @@ Also reported (``decode``): one 16-slot decode step over 48 G
 (fused conv + gates + recurrence + gated RMSNorm per layer, slot-indexed pools), replayed from a
 CUDA graph, in microseconds per step with its HBM roofline.
 
-``--impl reference`` times the CPU restatement of the reference's torch path (the oracle
-port) on this host's cores over a bounded sample of the same workload.
+``--impl reference`` times the reference's own torch prefill (fast_chunk_gated_delta_rule_v2, installed
+into oracle/_ref by oracle/install_ref.py; its torch restatement when that is absent) on this host's
+cores over a bounded sample of the same workload.
 
-Multi-GPU (torchrun, one rank per GPU): every rank runs its own replica of the workload
+Multi-GPU (torchrun, one rank per GPU): every rank runs its own replica of the same seeded workload
 (weak scaling, no collective on the data path); value = all ranks' tokens / max rank time.
 
 Also reported (``model``, BASELINE configs 3/4; ``--no-model`` skips it): the ~27B hybrid (64 layers,
@@ -100,6 +101,13 @@ def make_prefill_workload(seed: int):
     init = torch.randn(N_SEQ, HV, D, D, generator=g) * 0.02
     cu = torch.tensor([0] + np.cumsum(lens).tolist(), dtype=torch.int32)
     return dict(lens=lens, T=T, q=q, k=k, v=v, g=gg, beta=beta, init=init, cu=cu)
+
+
+def workload_config(w):
+    """The config block both arms print for the config-1 workload."""
+    return {"workload": "config1: GDN chunk prefill, 16 packed ragged seqs U[200,1200], Hk=16 Hv=48 dk=dv=128, "
+                        "chunk 64, bf16 q/k/v, fp32 state N(0,0.02) from a slot pool",
+            "total_tokens_per_gpu": w["T"]}
 
 
 def prefill_flops(lens):
@@ -204,12 +212,28 @@ def allreduce_sum(x: float, world: int) -> float:
 
 
 # ----------------------------------------------------------------------------- CPU legs
+def cpu_kind():
+    """'reference' when the reference's own modules are installed in oracle/_ref (oracle/install_ref.py),
+    else 'port' (the torch restatement oracle/gdn_torch_cpu.py, pinned to the same golden vectors)."""
+    from oracle import ref_cpu
+    return "reference" if ref_cpu.available() else "port"
+
+
 def cpu_prefill_sample(w, seconds: float):
-    """The reference's prefill path on the host cores: the torch restatement (oracle/gdn_torch_cpu.py)
-    of fast_chunk_gated_delta_rule_v2 (src/gdn_chunk_fast2.py:11-62) in the reference's dtypes, one
-    sequence per call as TPEngine.prefill does, over the workload's sequences in order (repeated
-    passes) until ~`seconds` elapse."""
+    """The reference's prefill path on the host cores: its own fast_chunk_gated_delta_rule_v2
+    (src/gdn_chunk_fast2.py:11-62, from oracle/_ref) -- or, without it, the torch restatement -- in
+    the reference's dtypes, one sequence per call as TPEngine.prefill does, over the workload's
+    sequences in order (repeated passes) until ~`seconds` elapse."""
     from oracle import gdn_torch_cpu as TC
+    from oracle import ref_cpu
+    if ref_cpu.available():
+        def rule(q, k, v, g, b, init):
+            return ref_cpu.chunk_prefill(q, k, v, g, b, init)
+        what = "the reference's own fast_chunk_gated_delta_rule_v2 (src/gdn_chunk_fast2.py)"
+    else:
+        def rule(q, k, v, g, b, init):
+            return TC.chunk_gated_delta_rule(q, k, v, g, b, 64, init, True, True)
+        what = "the torch restatement of src/gdn_chunk_fast2.py"
     r = HV // HK
     nseq = len(w["lens"])
     toks, used, el = 0, 0, 0.0
@@ -221,21 +245,24 @@ def cpu_prefill_sample(w, seconds: float):
             s, e = int(w["cu"][b]), int(w["cu"][b + 1])
             q = w["q"][s:e].repeat_interleave(r, dim=1)[None]
             k = w["k"][s:e].repeat_interleave(r, dim=1)[None]
-            TC.chunk_gated_delta_rule(q, k, w["v"][s:e][None], w["g"][s:e][None],
-                                      w["beta"][s:e].to(torch.bfloat16)[None], 64, w["init"][b][None], True, True)
+            rule(q, k, w["v"][s:e][None], w["g"][s:e][None], w["beta"][s:e].to(torch.bfloat16)[None],
+                 w["init"][b][None])
             toks += L
             used += 1
             el = time.perf_counter() - t0
     return toks / el, (f"{used} sequence calls ({used / nseq:.1f} passes over the {nseq} sequences, {toks} tokens), "
-                       f"one call per sequence of the torch restatement of src/gdn_chunk_fast2.py"), el
+                       f"one call per sequence of {what}"), el
 
 
 def cpu_decode_sample(seconds: float):
-    """The reference's decode layer on the host cores: the torch restatement (oracle/gdn_torch_cpu.py)
-    of CBEngine._gdn's operators (src/cb_engine.py:318-352: elem conv update, split, gates, l2norm,
-    recurrent_single_step with index_select / index_copy_ on the pools, gated RMSNorm) for 16 slots,
-    repeated over fresh layers until ~`seconds` elapse; returns µs per 48-layer step."""
+    """The reference's decode layer on the host cores: CBEngine._gdn's operators (src/cb_engine.py:
+    318-352: elem conv update, split, gates, l2norm, recurrent_single_step, gated RMSNorm) for 16
+    slots -- the reference's own functions from oracle/_ref, or without them the torch restatement
+    (with index_select / index_copy_ on the pools) -- repeated over fresh layers until ~`seconds`
+    elapse; returns µs per 48-layer step."""
     from oracle import gdn_torch_cpu as TC
+    from oracle import ref_cpu
+    own = ref_cpu.available()
     g = torch.Generator(device="cpu").manual_seed(1234)
     n, bf = DEC_SLOTS, torch.bfloat16
     layers, el = 0, 0.0
@@ -253,13 +280,19 @@ def cpu_decode_sample(seconds: float):
             norm_w = (1 + 0.1 * torch.randn(D, generator=g)).to(bf)
             slot = torch.randperm(n, generator=g)
             t_l = time.perf_counter()
-            TC.decode_layer(mixed, z, a, b, A_log, dt_bias, conv_w, conv_pool, rec_pool, slot, norm_w, HK, HV, D)
+            if own:
+                ref_cpu.decode_layer(mixed, z, a, b, A_log, dt_bias, conv_w, conv_pool, rec_pool, norm_w, HK, HV, D)
+            else:
+                TC.decode_layer(mixed, z, a, b, A_log, dt_bias, conv_w, conv_pool, rec_pool, slot, norm_w, HK, HV,
+                                D)
             el += time.perf_counter() - t_l
             layers += 1
             if time.perf_counter() - t0 >= seconds:
                 break
-    return el / layers * DEC_LAYERS * 1e6, (f"{layers} layers of 16 slots of the torch restatement of "
-                                            f"src/cb_engine.py:318-352, timed per layer, x {DEC_LAYERS}")
+    what = ("the reference's own elem_conv_update / recurrent_single_step with HF's gated norm" if own
+            else "the torch restatement")
+    return el / layers * DEC_LAYERS * 1e6, (f"{layers} layers of 16 slots of {what} (src/cb_engine.py:318-352), "
+                                            f"timed per layer, x {DEC_LAYERS}")
 
 
 def cpu_cores() -> int:
@@ -270,7 +303,8 @@ def cpu_cores() -> int:
 
 
 def run_reference(args, world, rank):
-    """--impl reference: the reference's torch path, restated (oracle/gdn_torch_cpu.py), on the host cores."""
+    """--impl reference: the reference's own torch prefill (from oracle/_ref; the restatement when it is
+    absent) on the host cores, every thread it can use."""
     if rank != 0:
         return
     w = make_prefill_workload(args.seed)
@@ -288,9 +322,8 @@ def run_reference(args, world, rank):
             "warmup": args.warmup, "ms_per_step": 1000.0 * w["T"] / value, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "impl": "reference",
-            "config": {"workload": "config1: GDN chunk prefill, 16 ragged seqs U[200,1200], Hk=16 Hv=48 d=128",
-                       "total_tokens": w["T"], "parallelism": "cpu"},
-            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cpu_cores(), "kind": "port",
+            "config": dict(workload_config(w), parallelism="cpu"),
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cpu_cores(), "kind": cpu_kind(),
                              "sample": samples},
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -331,7 +364,7 @@ def run_ours(args, world, rank, local):
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     stream = torch.cuda.current_stream()
-    w = make_prefill_workload(args.seed + rank)
+    w = make_prefill_workload(args.seed)          # every replica runs the same seeded workload
     T = w["T"]
     # ---- device-resident inputs
     q, k, v = w["q"].to(dev), w["k"].to(dev), w["v"].to(dev)
@@ -379,11 +412,9 @@ def run_ours(args, world, rank, local):
         "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded; config-1 distributions; no dataset or weights needed)",
-        "config": {"workload": "config1: GDN chunk prefill, 16 packed ragged seqs U[200,1200], Hk=16 Hv=48 "
-                               "dk=dv=128, chunk 64, bf16 q/k/v, fp32 state N(0,0.02) from a slot pool",
-                   "total_tokens_per_gpu": T, "chunks_per_head": chunks,
-                   "l2": f"inputs larger than L2 ({algo_bytes / 1e6:.0f} MB touched per step > 126 MB)",
-                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
+        "config": dict(workload_config(w), chunks_per_head=chunks,
+                       l2=f"inputs larger than L2 ({algo_bytes / 1e6:.0f} MB touched per step > 126 MB)",
+                       parallelism=f"replicas x{world}" if world > 1 else "single GPU"),
         "roofline": {"bound": "tensor", "achieved": achieved_tflops, "peak": tc_peak, "unit": "TFLOP/s",
                      "frac": achieved_tflops / tc_peak, "peak_source": peak_src + " (bf16 burst)",
                      "traffic": traffic, "algorithmic_flops_per_launch": flops,
@@ -404,11 +435,11 @@ def run_ours(args, world, rank, local):
     if rank == 0 and world == 1 and not args.no_cpu:
         torch.set_num_threads(cpu_cores())
         v_cpu, sample, el = cpu_prefill_sample(w, args.cpu_seconds)
-        line["cpu_baseline"] = {"value": v_cpu, "unit": "tokens/s", "cores": cpu_cores(), "kind": "port",
+        line["cpu_baseline"] = {"value": v_cpu, "unit": "tokens/s", "cores": cpu_cores(), "kind": cpu_kind(),
                                 "sample": sample + f", {el:.1f} s"}
         if decode is not None:
             us_cpu, dsample = cpu_decode_sample(max(2.0, args.cpu_seconds / 3))
-            line["decode"]["cpu_baseline"] = {"us_per_step": us_cpu, "cores": cpu_cores(), "kind": "port",
+            line["decode"]["cpu_baseline"] = {"us_per_step": us_cpu, "cores": cpu_cores(), "kind": cpu_kind(),
                                               "sample": dsample}
     if rank == 0:
         print(json.dumps(line), flush=True)

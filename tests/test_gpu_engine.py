@@ -174,3 +174,34 @@ def test_patch_model_hf_forward_matches_unpatched(setup):
     assert patch.patch_model(m2, fast_gdn=True, gdn_v2=True) == 3
     got = run(m2)
     assert (got - ref).abs().max().item() < 0.25
+
+
+def test_engine_raises_on_device_error_flag(setup):
+    """A slot index outside the pools reaches the GDN kernels (decode and prefill): they record
+    error 1 in the engine's device flag and leave every pool row as it was, and the engine raises
+    RuntimeError at the step's own host read instead of returning silent garbage."""
+    model, _ = setup
+    eng = _engine(model)
+    g = torch.Generator().manual_seed(5)
+    ids = torch.randint(0, model.config.text_config.vocab_size, (1, 9), generator=g)
+    eng.prefill(0, ids)
+    eng.check_errors()                                   # a clean step leaves the flag at 0
+    pools = [t.clone() for t in eng.rec.values()] + [t.clone() for t in eng.conv.values()]
+    eng._pos.zero_()
+    eng._slot.fill_(eng.N + 5)                           # past the scratch row: out of range
+    with torch.inference_mode():
+        out = eng._core(8)
+    torch.cuda.synchronize()
+    assert int(out[-1]) == 1                             # the flag rides with the step's tokens
+    after = [t for t in eng.rec.values()] + [t for t in eng.conv.values()]
+    assert all(torch.equal(a, b) for a, b in zip(pools, after))
+    with pytest.raises(RuntimeError, match="slot index"):
+        eng.check_errors()
+    eng.check_errors()                                   # raising clears the flag
+    # the same through the public prefill call: the GDN layers come first in this model, their
+    # kernels flag the slot before any host-side indexing of the attention cache
+    assert model.config.text_config.layer_types[0] == "linear_attention"
+    with pytest.raises((RuntimeError, IndexError)):
+        eng.prefill_batch([eng.N + 3], [ids])
+    eng._err.zero_()
+    assert eng.decode_step([0], [3])                     # the engine still runs after the error

@@ -90,6 +90,16 @@ def _rank(rank, world, port, out_path):
         # graph replay (all-reduces inside the graph) == eager, bit for bit on this rank
         eager_toks = [lg.argmax(-1).tolist() for lg in logits[1:]]
         assert graph_toks == eager_toks, (graph_toks, eager_toks)
+        # the LM head split by vocabulary (cross-rank packed argmax, captured in the graphs): the same
+        # tokens wherever the eager logits' top two are not a near-tie
+        vmodel = build_model(dev)
+        tp.shard_model(vmodel, rank, world, vocab_parallel=True)
+        vtoks = run(tp.TPEngine, vmodel, dev, True, tp=world)
+        for lg, vt in zip(logits[1:], vtoks):
+            top2 = np.sort(lg, axis=-1)[:, -2:]
+            for row, tok in enumerate(vt):
+                if top2[row, 1] - top2[row, 0] > 2e-2 * max(1.0, abs(top2[row, 1])):
+                    assert tok == int(lg[row].argmax()), (row, tok, int(lg[row].argmax()))
         if rank == 0:
             np.savez(out_path, *logits)
     finally:

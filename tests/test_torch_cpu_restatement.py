@@ -100,3 +100,21 @@ def test_decode_layer_matches_numpy_oracle():
     assert np.array_equal(cpt.float().numpy(), cp)
     assert np.abs(rpt.numpy() - rp).max() < 1e-4
     assert bf16_close(out.float().numpy(), ref)
+
+
+def test_installed_reference_reproduces_golden():
+    """When oracle/_ref holds the reference's own modules (oracle/install_ref.py), the baseline that
+    bench.py times is the code that wrote the golden vectors: it must reproduce them bit for bit."""
+    import pytest
+    from oracle import ref_cpu
+    if not ref_cpu.available():
+        pytest.skip("the reference is not installed in oracle/_ref")
+    d = load_golden("chunk_bf16.npz")
+    r = int(d["Hv"]) // int(d["Hk"])
+    for b in range(len(d["lens"])):
+        q = T(O.repeat_heads(d[f"q{b}"], r), bf)[None]
+        k = T(O.repeat_heads(d[f"k{b}"], r), bf)[None]
+        o, s = ref_cpu.chunk_prefill(q, k, T(d[f"v{b}"], bf)[None], T(d[f"g{b}"])[None], T(d[f"beta{b}"], bf)[None],
+                                     T(d[f"init{b}"])[None])
+        assert np.array_equal(o[0].float().numpy(), d[f"out{b}"])
+        assert np.array_equal(s[0].numpy(), d[f"state{b}"])

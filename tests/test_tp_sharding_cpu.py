@@ -81,10 +81,30 @@ def _worker(rank, world, port, q):
             assert torch.allclose(as_.o_proj(os_), af.o_proj(o), atol=1e-5)
             # MLP with its all-reduce equals the full MLP
             assert torch.allclose(ls[0].mlp(x), lf[0].mlp(x), atol=1e-5)
+            # vocabulary-parallel head: this rank's rows, and the cross-rank greedy pick equals the
+            # full argmax, ties included (the lowest id wins, as torch.argmax)
+            vp = tp.shard_model(_tiny_fp32(), rank, world, vocab_parallel=True)
+            V = 64 // world
+            h = torch.randn(7, 64)
+            assert torch.allclose(vp.lm_head(h), full.lm_head(h)[:, rank * V:(rank + 1) * V], atol=1e-6)
+            assert torch.equal(vp.lm_head.greedy(h), full.lm_head(h).argmax(-1))
+            w = full.lm_head.weight.detach().clone()
+            w[5] = w[60]                                     # ids 5 and 60 tie on every row
+            vp.lm_head.lin.weight.data.copy_(w[rank * V:(rank + 1) * V])
+            full.lm_head.weight.data.copy_(w)
+            h2 = torch.randn(6, 64)
+            h2[:3] = w[60] * 50                              # rows where the tied pair leads
+            assert torch.equal(vp.lm_head.greedy(h2), full.lm_head(h2).argmax(-1))
+            assert vp.lm_head.greedy(h2)[:3].tolist() == [5, 5, 5]
+            vp.lm_head.lin.weight.data.copy_(torch.abs(w[rank * V:(rank + 1) * V]))
+            full.lm_head.weight.data.copy_(torch.abs(w))
+            neg = -torch.abs(torch.randn(4, 64))             # all logits negative: the order still holds
+            assert (full.lm_head(neg) < 0).all()
+            assert torch.equal(vp.lm_head.greedy(neg), full.lm_head(neg).argmax(-1))
         q.put((rank, "ok"))
     except Exception as e:  # report to the parent instead of hanging it
         import traceback
-        q.put((rank, traceback.format_exc()[-300:]))
+        q.put((rank, traceback.format_exc()[-800:]))
     finally:
         if dist.is_initialized():
             dist.destroy_process_group()
