@@ -21,10 +21,13 @@ Multi-GPU (torchrun, one rank per GPU): every rank runs its own replica of the s
 (weak scaling, no collective on the data path); value = all ranks' tokens / max rank time.
 
 Also reported (``model``, BASELINE configs 3/4; ``--no-model`` skips it): the ~27B hybrid (64 layers,
-3 GDN : 1 attention, hidden 5120) with random bf16 weights run through the slot engine -- one
-packed prefill of the slots' prompts (lengths U[300,700], random token ids), then graph-replayed
-decode steps for every slot; with N ranks the model is head-sharded over all of them (TP = N,
-NCCL all-reduce after o_proj/out_proj/down_proj) with min(64, 16 N) slots (64 at N = 8).
+3 GDN : 1 attention, hidden 5120) with random bf16 weights run through the slot engine, serving the
+synthetic multi-turn request workload (prompts U[300,700], 1-6 turns of 512 greedy tokens, later
+turns append U[50,300] tokens) with continuous batching; ``--requests`` sets the request count (one
+per slot by default; the configs name 128 and 512).  With N ranks the model is head-sharded over all
+of them (TP = N, the LM head split by vocabulary) with min(64, 16 N) slots (64 at N = 8), and a
+``tp_parity`` gate (peer all-reduce bit-exactness, a 4-layer TP model against the single-GPU engine)
+runs first.
 """
 from __future__ import annotations
 
@@ -79,7 +82,10 @@ def parse():
     ap.add_argument("--no-model", action="store_true",
                     help="skip the config 3/4 model leg (the ~27B hybrid with random weights through the engine, "
                          "tensor-parallel over all ranks when launched with more than one)")
-    ap.add_argument("--model-steps", type=int, default=32, help="timed decode steps of the model leg")
+    ap.add_argument("--requests", type=int, default=0,
+                    help="requests of the model leg (0: one per slot; configs 3/4 name 128 / 512)")
+    ap.add_argument("--model-turns", type=int, default=6, help="most turns per request of the model leg")
+    ap.add_argument("--model-gen", type=int, default=512, help="greedy tokens per turn of the model leg")
     ap.add_argument("--model-allreduce", choices=["peer", "nccl"], default="peer",
                     help="TP decode sums: this library's peer-memory kernel or NCCL")
     return ap.parse_args()
@@ -199,6 +205,15 @@ def allreduce_max(x: float, world: int) -> float:
     import torch.distributed as dist
     t = torch.tensor([x], dtype=torch.float64, device="cuda")
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def allreduce_min(x: float, world: int) -> float:
+    if world <= 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MIN)
     return float(t.item())
 
 
@@ -450,16 +465,12 @@ def model_slots(world):
     return 16 if world <= 1 else min(64, 16 * world)
 
 
-def run_model(args, world, rank, local):
-    """Model leg (configs 3/4): random-init ~27B hybrid through the slot engine."""
+def build_model(text_cfg, dev, seed):
+    """Random-init bf16 Qwen3.5 (identical on every rank for the same seed)."""
     from transformers.models.qwen3_5.configuration_qwen3_5 import Qwen3_5Config
     from transformers.models.qwen3_5.modeling_qwen3_5 import Qwen3_5ForConditionalGeneration
-    eng_mod = importlib.import_module(f"{PKG}.engine")
-    tp_mod = importlib.import_module(f"{PKG}.tp")
-    dev = torch.device("cuda", local)
-    t_build = time.time()
-    torch.manual_seed(1234)                     # identical full model on every rank before sharding
-    cfg = Qwen3_5Config(text_config=MODEL_TEXT_CONFIG, vision_config=MODEL_VISION_CONFIG)
+    torch.manual_seed(seed)
+    cfg = Qwen3_5Config(text_config=text_cfg, vision_config=MODEL_VISION_CONFIG)
     prev = torch.get_default_dtype()
     torch.set_default_dtype(torch.bfloat16)
     try:
@@ -467,65 +478,234 @@ def run_model(args, world, rank, local):
             model = Qwen3_5ForConditionalGeneration(cfg)
     finally:
         torch.set_default_dtype(prev)
-    model = model.to(torch.bfloat16).eval()
+    return model.to(torch.bfloat16).eval()
+
+
+def model_decode_bytes(model, eng):
+    """(fixed bytes, bytes per context token) one decode step of ``eng`` moves on this rank: every
+    local weight of the decoder layers, the final norm and the (local) LM head, and every slot's GDN
+    recurrent state (read + write) and conv state; plus, per slot and attention layer, the KV rows
+    0..ctx that the step reads."""
+    lm = model.model.language_model
+    w = sum(p.numel() * p.element_size() for n, p in lm.named_parameters() if "embed_tokens" not in n)
+    w += sum(p.numel() * p.element_size() for p in model.lm_head.parameters())
+    st = sum(t[:eng.N].numel() * t.element_size() * 2 for t in eng.rec.values())
+    st += sum(t[:eng.N].numel() * t.element_size() * 2 for t in eng.conv.values())
+    kv = sum(t.shape[1] * t.shape[3] * 2 * t.element_size() for t in eng.kv_k.values())
+    return w + st, kv
+
+
+def model_prefill_flops(model, tokens, seqs):
+    """Approximate prefill FLOPs on this rank: 2 x (local matmul weights) per token, the GDN chunk
+    algebra (per 64-token chunk and local value head) and causal attention (QK^T and PV over the
+    causal half, per local head)."""
+    lm = model.model.language_model
+    cfg = model.config.text_config
+    mat = sum(p.numel() for n, p in lm.named_parameters() if p.dim() == 2 and "embed_tokens" not in n)
+    f = 2.0 * mat * tokens + 2.0 * sum(p.numel() for p in model.lm_head.parameters()) * len(seqs)
+    for layer, kind in zip(lm.layers, cfg.layer_types):
+        if kind == "full_attention":
+            at = layer.self_attn
+            nh = at.q_proj.weight.shape[0] // (2 * at.head_dim)
+            f += sum(2.0 * L * L * at.head_dim * nh for L in seqs)
+        else:
+            hv = layer.linear_attn.num_v_heads
+            f += sum(math.ceil(L / CHUNK) for L in seqs) * hv * FLOP_PER_HEAD_CHUNK
+    return f
+
+
+def tp_parity(world, rank, local):
+    """Correctness gate of the tensor-parallel path, run before the timed model leg on N > 1 ranks.
+
+    (1) The peer-memory all-reduce on the decode size [slots, hidden] bf16: bit-identical to the fp32
+        sum of all ranks' inputs in rank order rounded once to bf16, and within one bf16 rounding of
+        NCCL's all-reduce.
+    (2) A 4-layer model with the config-3 shapes (3 GDN : 1 attention, 24 q / 4 KV heads, so TP 8
+        replicates KV heads; the LM head split by vocabulary): the TP engine over all ranks against
+        the single-GPU engine on rank 0 with the same weights and feed (three prompts, then two
+        teacher-forced decode steps): the logits of the prefill and of each decode step, gathered from
+        the ranks' vocabulary slices, and the GDN slot states gathered from the ranks' head shards,
+        within the engine test's bf16 tolerance (2e-2 + 2e-2 max|ref|)."""
+    import torch.distributed as dist
+    eng_mod = importlib.import_module(f"{PKG}.engine")
+    tp_mod = importlib.import_module(f"{PKG}.tp")
+    dev = torch.device("cuda", local)
+    res = {}
+    # ---- (1) peer all-reduce
+    slots = model_slots(world)
+    H = MODEL_TEXT_CONFIG["hidden_size"]
+    xs = [torch.randn(slots, H, generator=torch.Generator().manual_seed(900 + r)).to(torch.bfloat16)
+          for r in range(world)]
+    ref = torch.zeros(slots, H)
+    for x in xs:
+        ref += x.float()
+    ref = ref.to(torch.bfloat16).to(dev)
+    ar = tp_mod.PeerAllReduce(slots * H, dev)
+    y = xs[rank].to(dev).clone()
+    ar(y)
+    z = xs[rank].to(dev).clone()
+    dist.all_reduce(z)
+    torch.cuda.synchronize()
+    ar_err = int(ar.err.item())
+    ar.close()
+    bit = bool(torch.equal(y, ref)) and ar_err == 0
+    ulps = (z.float() - ref.float()).abs() / torch.clamp(ref.float().abs(), min=1e-3) * 128
+    res["allreduce"] = {"shape": [slots, H], "bitexact_vs_fp32_rank_order": bit, "err_flag": ar_err,
+                        "max_vs_nccl_bf16_ulps": float(ulps.max().item())}
+    # ---- (2) 4-layer model
+    cfg = dict(MODEL_TEXT_CONFIG, num_hidden_layers=4,
+               layer_types=["linear_attention", "linear_attention", "linear_attention", "full_attention"])
+    g = torch.Generator().manual_seed(77)
+    prompts = [torch.randint(0, cfg["vocab_size"], (1, L), generator=g) for L in (157, 64, 301)]
+    feed = [torch.randint(0, cfg["vocab_size"], (3,), generator=g).tolist() for _ in range(2)]
+
+    def run(eng, head):
+        logits = []
+        hk = head.register_forward_hook(lambda m, i, o: logits.append(o.detach().float()))
+        eng.prefill_batch([0, 1, 2], prompts)
+        for t in feed:
+            eng.decode_step([0, 1, 2], t)
+        hk.remove()
+        return logits, [eng.rec[i][:3].clone() for i in sorted(eng.rec)]
+
+    ref_logits = ref_states = None
+    if rank == 0:
+        full = build_model(cfg, dev, seed=4242)
+        e1 = eng_mod.CBEngine(full, 3, 512, dev, graph_decode=False)
+        ref_logits, ref_states = run(e1, full.lm_head)
+        del e1, full
+        torch.cuda.empty_cache()
+    model = build_model(cfg, dev, seed=4242)
+    tp_mod.shard_model(model, rank, world, vocab_parallel=True)
+    eng = tp_mod.TPEngine(model, 3, 512, dev, world, graph_decode=False)
+    logits, states = run(eng, model.lm_head.lin)            # this rank's vocabulary slice
+    eng.check_errors()
+    eng.close()
+    full_logits, full_states = [], []
+    for lg in logits:
+        parts = [torch.empty_like(lg) for _ in range(world)]
+        dist.all_gather(parts, lg.contiguous())
+        full_logits.append(torch.cat(parts, dim=-1))
+    for st in states:
+        parts = [torch.empty_like(st) for _ in range(world)]
+        dist.all_gather(parts, st.contiguous())
+        full_states.append(torch.cat(parts, dim=1))          # value heads in rank order
+    ok = bit
+    if rank == 0:
+        le = [float((a - b).abs().max().item()) for a, b in zip(full_logits, ref_logits)]
+        lt = [2e-2 + 2e-2 * float(b.abs().max().item()) for b in ref_logits]
+        se = max(float((a - b).abs().max().item()) for a, b in zip(full_states, ref_states))
+        st_tol = 2e-2 + 2e-2 * max(float(b.abs().max().item()) for b in ref_states)
+        ok = ok and len(le) == 3 and all(e <= t for e, t in zip(le, lt)) and se <= st_tol
+        res["model"] = {"layers": 4, "hidden": cfg["hidden_size"], "vocab_parallel_head": True,
+                        "prefill_logits_err": le[0], "decode_logits_err": le[1:], "logits_tol": lt,
+                        "gdn_state_err": se, "gdn_state_tol": st_tol}
+    flag = torch.tensor([1 if ok else 0], dtype=torch.int32, device=dev)
+    dist.broadcast(flag, 0)
+    res["ok"] = bool(flag.item())
+    del model, eng
+    torch.cuda.empty_cache()
+    return res
+
+
+def run_model(args, world, rank, local):
+    """Model leg (configs 3/4): the random-init ~27B hybrid through the slot engine, serving the
+    synthetic multi-turn request workload with continuous batching (serve.run_requests)."""
+    eng_mod = importlib.import_module(f"{PKG}.engine")
+    tp_mod = importlib.import_module(f"{PKG}.tp")
+    serve = importlib.import_module(f"{PKG}.serve")
+    dev = torch.device("cuda", local)
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except (OSError, ValueError):
+        pass
+    hbm_peak = peaks.get("hbm_gbs", 6650.0)
+    tc_peak = peaks.get("bf16_tflops_sustained", 1400.0)
+    peak_src = "of measured" if peaks else "of fallback"
+    parity = tp_parity(world, rank, local) if world > 1 else None
+    t_build = time.time()
+    model = build_model(MODEL_TEXT_CONFIG, dev, seed=1234)   # identical full model on every rank
     params = sum(p.numel() for n, p in model.named_parameters() if "visual" not in n)
     if world > 1:
-        tp_mod.shard_model(model, rank, world)
+        tp_mod.shard_model(model, rank, world, vocab_parallel=True)
     # as the reference's runs do before building the engine (src/cb_run.py:158): the layer RMSNorms
     # and the GDN plug-in points of the HF modules go to this library's kernels
     importlib.import_module(f"{PKG}.patch").patch_model(model, fast_gdn=True, gdn_v2=True)
     torch.cuda.empty_cache()
     slots = model_slots(world)
-    t_max = 1024
+    n_req = args.requests if args.requests > 0 else slots
+    reqs = serve.synthetic_requests(n_req, MODEL_TEXT_CONFIG["vocab_size"], seed=4321, max_turns=args.model_turns)
+    bucket = eng_mod.GRAPH_BUCKET
+    t_max = -(-(serve.max_context(reqs, args.model_gen) + 1) // bucket) * bucket
     peer = args.model_allreduce == "peer"
     eng = (tp_mod.TPEngine(model, slots, t_max, dev, world, graph_decode=True, peer_allreduce=peer) if world > 1
            else eng_mod.CBEngine(model, slots, t_max, dev, graph_decode=True))
-    g = torch.Generator(device="cpu").manual_seed(4321)
-    lens = torch.randint(MODEL_PLEN[0], MODEL_PLEN[1] + 1, (slots,), generator=g).tolist()
-    prompts = [torch.randint(0, MODEL_TEXT_CONFIG["vocab_size"], (1, L), generator=g) for L in lens]
     build_s = time.time() - t_build
-    # warm-up: the same packed prefill (GEMM shapes, cuBLAS heuristics and kernel loading, allocator),
-    # slots freed again; then the timed packed prefill of every slot
-    eng.prefill_batch(list(range(slots)), prompts)
-    for s_ in range(slots):
-        eng.free(s_)
+    # warm-up: single-turn requests of the same prompt lengths through the same loop (GEMM shapes,
+    # cuBLAS heuristics, kernel loading), a few tokens each
+    warm = serve.synthetic_requests(slots, MODEL_TEXT_CONFIG["vocab_size"], seed=99, max_turns=1)
+    serve.run_requests(eng, warm, gen_tokens=8)
     torch.cuda.synchronize()
     barrier(world)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    toks = eng.prefill_batch(list(range(slots)), prompts)
-    e1.record()
-    torch.cuda.synchronize()
-    pre_ms = allreduce_max(e0.elapsed_time(e1), world)
-    all_slots = list(range(slots))
-    for _ in range(max(3, args.warmup)):
-        toks = eng.decode_step(all_slots, toks)
+    fixed_b, ctx_b = model_decode_bytes(model, eng)
+    acc = {"dec_bytes": 0.0, "pre_flops": 0.0}
+
+    def on_step(kind, dt, info):
+        if kind == "decode":
+            acc["dec_bytes"] += fixed_b + ctx_b * sum(c + 1 for c in info["ctx"])
+        else:
+            acc["pre_flops"] += model_prefill_flops(model, info["tokens"], info["seqs"])
+
+    st = serve.run_requests(eng, reqs, gen_tokens=args.model_gen, on_step=on_step)
     torch.cuda.synchronize()
     barrier(world)
-    e0.record()
-    for _ in range(args.model_steps):
-        toks = eng.decode_step(all_slots, toks)
-    e1.record()
-    torch.cuda.synchronize()
-    dec_ms = allreduce_max(e0.elapsed_time(e1), world) / args.model_steps
+    eng.check_errors()
     if world > 1:
-        eng.check_errors()
         eng.close()                              # graphs and peer buffers go before the process group
     else:
         eng._graphs.clear()
         eng._graph_out.clear()
+    mk = allreduce_max(st["makespan_s"], world)
+    dec_s = allreduce_max(st["decode_s"], world)
+    pre_s = allreduce_max(st["prefill_s"], world)
+    dec_gbs = acc["dec_bytes"] / st["decode_s"] / 1e9 if st["decode_s"] > 0 else 0.0
+    pre_tf = acc["pre_flops"] / st["prefill_s"] / 1e12 if st["prefill_s"] > 0 else 0.0
+    dec_gbs = allreduce_min(dec_gbs, world)
+    pre_tf = allreduce_min(pre_tf, world)
     del eng, model
     torch.cuda.empty_cache()
-    n_pre = sum(lens)
-    return {"config": "config 3" if world <= 1 else f"config 4 (TP {world})",
-            "params": params, "layers": MODEL_TEXT_CONFIG["num_hidden_layers"], "tp": world, "slots": slots,
-            "prefill_tokens": n_pre, "prefill_ms": pre_ms, "prefill_tokens_per_s": n_pre / (pre_ms / 1e3),
-            "decode_steps": args.model_steps, "decode_ms_per_step": dec_ms,
-            "decode_tokens_per_s": slots / (dec_ms / 1e3), "graph": True, "weights": "random-init bf16",
-            "allreduce": ("none" if world <= 1 else
-                          "gdn_allreduce (peer memory) for decode, NCCL for prefill" if peer else "NCCL"),
-            "prompts": f"uniform random token ids, lengths U[{MODEL_PLEN[0]},{MODEL_PLEN[1]}]",
-            "build_s": build_s}
+    out = {"config": "config 3" if world <= 1 else f"config 4 (TP {world})",
+           "params": params, "layers": MODEL_TEXT_CONFIG["num_hidden_layers"], "tp": world, "slots": slots,
+           "requests": n_req, "requests_in_config": 128 if world <= 1 else 512,
+           "workload": (f"synthetic multi-turn: prompts U[{MODEL_PLEN[0]},{MODEL_PLEN[1]}] random ids, 1-"
+                        f"{args.model_turns} turns, {args.model_gen} greedy tokens per turn, later turns append "
+                        "U[50,300] ids and re-prefill the whole conversation; FIFO continuous batching "
+                        "(src/cb_run.py:254-378 scheduling)"),
+           "turns": st["turns"], "t_max": t_max, "makespan_s": mk,
+           "tokens_per_s": (st["prefill_tokens"] + st["decode_tokens"]) / mk,
+           "prefill_tokens": st["prefill_tokens"], "prefill_calls": st["prefill_calls"], "prefill_s": pre_s,
+           "prefill_tokens_per_s": st["prefill_tokens"] / pre_s,
+           "decode_steps": st["decode_steps"], "decode_tokens": st["decode_tokens"], "decode_s": dec_s,
+           "decode_ms_per_step": 1e3 * dec_s / max(1, st["decode_steps"]),
+           "decode_tokens_per_s": st["decode_tokens"] / dec_s,
+           "roofline": {"decode": {"bound": "hbm", "achieved": dec_gbs, "peak": hbm_peak, "unit": "GB/s",
+                                   "frac": dec_gbs / hbm_peak, "peak_source": peak_src,
+                                   "bytes": "per rank per step: local weights + LM head, KV rows read, "
+                                            "GDN/conv state read + write; slowest rank"},
+                        "prefill": {"bound": "tensor", "achieved": pre_tf, "peak": tc_peak, "unit": "TFLOP/s",
+                                    "frac": pre_tf / tc_peak, "peak_source": peak_src + " (bf16 sustained)",
+                                    "flops": "per rank, approximate: 2 x matmul weights x tokens + GDN chunk "
+                                             "algebra + causal attention; slowest rank"}},
+           "timing": "wall clock per engine call (each ends with its host read of the tokens), max over ranks",
+           "graph": True, "weights": "random-init bf16",
+           "allreduce": ("none" if world <= 1 else
+                         "gdn_allreduce (peer memory) for decode, NCCL for prefill" if peer else "NCCL"),
+           "lm_head": "vocabulary-parallel" if world > 1 else "full", "build_s": build_s}
+    if parity is not None:
+        out["tp_parity"] = parity
+    return out
 
 
 def run_e2e(ops, w, q, k, v, g, beta, cu, pool, slot, use_init, out, args, world, stream, tot_tokens):
