@@ -77,6 +77,8 @@ def parse():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-decode", action="store_true", help="skip the config-2 decode measurement")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
+    ap.add_argument("--decode-layers", type=int, default=DEC_LAYERS,
+                    help="GDN layers in the decode leg's step (48 in config 2; fewer for short profiler captures)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="target CPU-baseline sample time")
     ap.add_argument("--no-model", action="store_true",
@@ -770,7 +772,7 @@ def run_e2e(ops, w, q, k, v, g, beta, cu, pool, slot, use_init, out, args, world
 
 def run_decode(ops, dev, args, world, hbm_peak, peak_src):
     g = torch.Generator(device="cpu").manual_seed(1234)
-    n, L = DEC_SLOTS, DEC_LAYERS
+    n, L = DEC_SLOTS, args.decode_layers
     bf = torch.bfloat16
     layers = []
     for _ in range(L):
@@ -822,7 +824,7 @@ def run_decode(ops, dev, args, world, hbm_peak, peak_src):
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                          "frac": achieved / hbm_peak, "peak_source": peak_src,
                          "algorithmic_bytes_per_step": total,
-                         "traffic": load_traffic().get("gdn_decode_step")},
+                         "traffic": (load_traffic().get("gdn_decode_layer", 0.0) * L) or None},
             "gpu_launches": args.steps * L * 2}
 
 
