@@ -33,6 +33,9 @@ SIGNATURES = {
     "gdn_decode_layer_workspace_size": (_sz, [_i32, _i32, _i32, _i32, _i32, _i32]),
     "gdn_decode_layer": (_i32, [_vp, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _vp, _f32,
                                 _vp, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _vp, _sz, _i32, _vp, _vp]),
+    "gdn_decode_layer_rows": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _vp, _i64, _vp, _vp, _vp, _vp, _vp, _vp,
+                                     _vp, _i64, _vp, _f32, _vp, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _vp, _sz,
+                                     _i32, _vp, _vp]),
     "gdn_decode_layer_noalloc_max_bytes": (_sz, []),
     "gdn_decode_layer_noalloc_max_ticket_bytes": (_sz, []),
     "gdn_decode_layer_noalloc": (_i32, [_vp, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _vp,

@@ -43,6 +43,8 @@ struct RecParams {
   void* out;
   int64_t o_sb, o_st;
   const void* z;       // gate for the fused gated RMSNorm [B,Hv,dv] (null: plain output)
+  int64_t z_rs;        // element stride between z's rows b (Hv * dv when contiguous)
+  int64_t a_rs, b_rs;  // element strides between the rows b of a_raw / b_raw (Hv when contiguous)
   const void* norm_w;  // [dv]
   float eps;
   // fused conv update (decode layer, T = 1): q/k/v are the silu(conv) of mixed_qkv [B, C] with the
@@ -238,8 +240,8 @@ __global__ void __launch_bounds__(RecShape<DK, DV>::NT, 2) recurrent_kernel(RecP
     if (warp == 3 && lane == 0) {
       float beta, g;
       if (p.a_raw) {
-        const float a = Io<T>::ld(reinterpret_cast<const T*>(p.a_raw) + int64_t(b) * p.Hv + h);
-        const float braw = Io<T>::ld(reinterpret_cast<const T*>(p.b_raw) + int64_t(b) * p.Hv + h);
+        const float a = Io<T>::ld(reinterpret_cast<const T*>(p.a_raw) + int64_t(b) * p.a_rs + h);
+        const float braw = Io<T>::ld(reinterpret_cast<const T*>(p.b_raw) + int64_t(b) * p.b_rs + h);
         beta = Io<T>::rnd(sigmoid_f(braw));
         g = -expf(p.A_log[h]) * softplus_f(a + p.dt_bias[h]);
       } else {
@@ -309,7 +311,7 @@ __global__ void __launch_bounds__(RecShape<DK, DV>::NT, 2) recurrent_kernel(RecP
 #pragma unroll
         for (int i = 0; i < DV / 32; ++i) tot += snorm[i];
         const float rinv = 1.0f / sqrtf(tot / float(DV) + p.eps);
-        const T* zr = reinterpret_cast<const T*>(p.z) + (int64_t(b) * p.Hv + h) * DV;
+        const T* zr = reinterpret_cast<const T*>(p.z) + int64_t(b) * p.z_rs + int64_t(h) * DV;
         const float w = Io<T>::ld(reinterpret_cast<const T*>(p.norm_w) + tid);
         o = Io<T>::rnd(w * Io<T>::rnd(o * rinv)) * silu_f(Io<T>::ld(zr + tid));
       }
@@ -438,8 +440,8 @@ __global__ void __launch_bounds__(dec::D) decode_prep_kernel(RecParams p, T* pre
   Io<T>::st(prep + int64_t(b) * p.C + c, y);
   if (row >= 2 * p.Hk && tid == 0) {
     const int h = row - 2 * p.Hk;
-    const float a = Io<T>::ld(reinterpret_cast<const T*>(p.a_raw) + int64_t(b) * p.Hv + h);
-    const float braw = Io<T>::ld(reinterpret_cast<const T*>(p.b_raw) + int64_t(b) * p.Hv + h);
+    const float a = Io<T>::ld(reinterpret_cast<const T*>(p.a_raw) + int64_t(b) * p.a_rs + h);
+    const float braw = Io<T>::ld(reinterpret_cast<const T*>(p.b_raw) + int64_t(b) * p.b_rs + h);
     float* gt = gates + (int64_t(b) * p.Hv + h) * 4;
     gt[0] = -expf(p.A_log[h]) * softplus_f(a + p.dt_bias[h]);
     gt[1] = Io<T>::rnd(sigmoid_f(braw));
@@ -500,7 +502,8 @@ __global__ void __launch_bounds__(dec::kThreads, 1) decode_state_kernel(RecParam
     bulk_load(dst + 16, row + hk * D, kRowBytes, bar);
     bulk_load(dst + 16 + kRowBytes, row + (p.Hk + hk) * D, kRowBytes, bar);
     bulk_load(dst + 16 + 2 * kRowBytes, row + (2 * p.Hk + h) * D, kRowBytes, bar);
-    bulk_load(dst + 16 + 3 * kRowBytes, reinterpret_cast<const T*>(p.z) + int64_t(it) * D, kRowBytes, bar);
+    bulk_load(dst + 16 + 3 * kRowBytes, reinterpret_cast<const T*>(p.z) + int64_t(b) * p.z_rs + int64_t(h) * D,
+              kRowBytes, bar);
   };
   if (tid == kCopyTid) {
     // item 0 first: the states do not depend on the prep kernel, its q/k/v rows and gates do; the
@@ -756,42 +759,74 @@ extern "C" size_t gdn_decode_layer_workspace_size(int n, int Hk, int Hv, int dk,
   return (bytes + 255) & ~size_t(255);
 }
 
-extern "C" int gdn_decode_layer(const void* mixed_qkv, int64_t mixed_rs, const void* z, const void* a,
-                                const void* b, const float* A_log, const float* dt_bias, const void* conv_w,
-                                const void* conv_b, void* conv_pool, float* rec_pool, const int32_t* slot_idx,
-                                int64_t n_slots, const void* norm_w, float eps, void* out, int n, int Hk,
-                                int Hv, int dk, int dv, int K, int conv_mode, void* workspace,
-                                size_t workspace_bytes, int dtype, int32_t* err_flag, void* stream) {
-  using namespace gdn;
-  int rc = check_heads("gdn_decode_layer", n, Hk, Hv, dk, dv);
+namespace gdn {
+// Body of gdn_decode_layer and gdn_decode_layer_rows: z, a and b rows `z_rs`, `a_rs`, `b_rs` elements
+// apart (Hv * dv, Hv and Hv for contiguous tensors).
+static int decode_layer_impl(const char* fn, const void* mixed_qkv, int64_t mixed_rs, const void* z, int64_t z_rs,
+                             const void* a, int64_t a_rs, const void* b, int64_t b_rs, const float* A_log,
+                             const float* dt_bias, const void* conv_w, const void* conv_b, void* conv_pool,
+                             float* rec_pool, const int32_t* slot_idx, int64_t n_slots, const void* norm_w, float eps,
+                             void* out, int n, int Hk, int Hv, int dk, int dv, int K, int conv_mode, void* workspace,
+                             size_t workspace_bytes, int dtype, int32_t* err_flag, void* stream) {
+  int rc = check_heads(fn, n, Hk, Hv, dk, dv);
   if (rc) return rc;
   if (n == 0) return GDN_OK;
   if (!mixed_qkv || !z || !a || !b || !A_log || !dt_bias || !conv_w || !conv_pool || !rec_pool || !norm_w || !out)
-    return fail(GDN_ERR_ARG, "gdn_decode_layer: null pointer");
-  if (n_slots < 1) return fail(GDN_ERR_ARG, "gdn_decode_layer: n_slots=%lld", (long long)n_slots);
-  if (dtype != GDN_BF16 && dtype != GDN_F32) return fail(GDN_ERR_DTYPE, "gdn_decode_layer: dtype %d", dtype);
-  if (K < 1 || K > 8) return fail(GDN_ERR_SHAPE, "gdn_decode_layer: K=%d (1..8)", K);
-  if (conv_mode != GDN_CONV_HF && conv_mode != GDN_CONV_ELEM)
-    return fail(GDN_ERR_ARG, "gdn_decode_layer: conv mode %d", conv_mode);
+    return fail(GDN_ERR_ARG, "%s: null pointer", fn);
+  if (n_slots < 1) return fail(GDN_ERR_ARG, "%s: n_slots=%lld", fn, (long long)n_slots);
+  if (dtype != GDN_BF16 && dtype != GDN_F32) return fail(GDN_ERR_DTYPE, "%s: dtype %d", fn, dtype);
+  if (K < 1 || K > 8) return fail(GDN_ERR_SHAPE, "%s: K=%d (1..8)", fn, K);
+  if (conv_mode != GDN_CONV_HF && conv_mode != GDN_CONV_ELEM) return fail(GDN_ERR_ARG, "%s: conv mode %d", fn, conv_mode);
+  if (z_rs < int64_t(Hv) * dv || a_rs < Hv || b_rs < Hv || mixed_rs < 2 * Hk * dk + Hv * dv)
+    return fail(GDN_ERR_ARG, "%s: row strides (mixed %lld, z %lld, a %lld, b %lld) shorter than a row", fn,
+                (long long)mixed_rs, (long long)z_rs, (long long)a_rs, (long long)b_rs);
   const size_t need = gdn_decode_layer_workspace_size(n, Hk, Hv, dk, dv, dtype);
   if (!workspace || workspace_bytes < need)
-    return fail(GDN_ERR_WORKSPACE, "gdn_decode_layer: workspace %zu bytes < %zu", workspace_bytes, need);
-  if (!aligned(rec_pool, 16) || !aligned(workspace, 16) || !aligned(z, 16))
-    return fail(GDN_ERR_ARG, "gdn_decode_layer: rec_pool, z and the workspace must be 16-byte aligned");
+    return fail(GDN_ERR_WORKSPACE, "%s: workspace %zu bytes < %zu", fn, workspace_bytes, need);
+  const int esz = dtype == GDN_BF16 ? 2 : 4;
+  // z rows move by 16-byte bulk copies
+  if (!aligned(rec_pool, 16) || !aligned(workspace, 16) || !aligned(z, 16) || (z_rs * esz) % 16 != 0)
+    return fail(GDN_ERR_ARG, "%s: rec_pool, z, z's row stride and the workspace must be 16-byte aligned", fn);
   // conv update of the slot's window + gates + l2norm + recurrence (in place on rec_pool[slot_idx])
   // + gated RMSNorm: two kernels for dk = dv = 128, one (ticket-ordered windows) for 64
   RecParams p{};
   p.mixed = mixed_qkv; p.mixed_rs = mixed_rs; p.conv_w = conv_w; p.conv_b = conv_b; p.conv_pool = conv_pool;
   p.tickets = reinterpret_cast<unsigned int*>(workspace);
   p.C = 2 * Hk * dk + Hv * dv; p.K = K; p.conv_mode = conv_mode;
-  p.a_raw = a; p.b_raw = b; p.A_log = A_log; p.dt_bias = dt_bias;
+  p.a_raw = a; p.b_raw = b; p.a_rs = a_rs; p.b_rs = b_rs; p.A_log = A_log; p.dt_bias = dt_bias;
   p.init_pool = rec_pool; p.init_slot = slot_idx; p.final_pool = rec_pool; p.final_slot = slot_idx;
   p.n_slots = n_slots;
   p.out = out; p.o_sb = int64_t(Hv) * dv; p.o_st = 0;
-  p.z = z; p.norm_w = norm_w; p.eps = eps;
+  p.z = z; p.z_rs = z_rs; p.norm_w = norm_w; p.eps = eps;
   p.B = n; p.T = 1; p.Hk = Hk; p.Hv = Hv; p.l2norm = 1; p.err = err_flag;
   if (dk == 128 && dv == 128)
     return dtype == GDN_BF16 ? launch_decode_layer<__nv_bfloat16>(p, workspace, as_stream(stream))
                              : launch_decode_layer<float>(p, workspace, as_stream(stream));
   return run_recurrent(p, dk, dv, dtype, as_stream(stream));
+}
+}  // namespace gdn
+
+extern "C" int gdn_decode_layer(const void* mixed_qkv, int64_t mixed_rs, const void* z, const void* a,
+                                const void* b, const float* A_log, const float* dt_bias, const void* conv_w,
+                                const void* conv_b, void* conv_pool, float* rec_pool, const int32_t* slot_idx,
+                                int64_t n_slots, const void* norm_w, float eps, void* out, int n, int Hk,
+                                int Hv, int dk, int dv, int K, int conv_mode, void* workspace,
+                                size_t workspace_bytes, int dtype, int32_t* err_flag, void* stream) {
+  const int64_t hv = Hv > 0 ? Hv : 0;
+  return gdn::decode_layer_impl("gdn_decode_layer", mixed_qkv, mixed_rs, z, hv * (dv > 0 ? dv : 0), a, hv, b, hv,
+                                A_log, dt_bias, conv_w, conv_b, conv_pool, rec_pool, slot_idx, n_slots, norm_w, eps,
+                                out, n, Hk, Hv, dk, dv, K, conv_mode, workspace, workspace_bytes, dtype, err_flag,
+                                stream);
+}
+
+extern "C" int gdn_decode_layer_rows(const void* mixed_qkv, int64_t mixed_rs, const void* z, int64_t z_rs,
+                                     const void* a, int64_t a_rs, const void* b, int64_t b_rs, const float* A_log,
+                                     const float* dt_bias, const void* conv_w, const void* conv_b, void* conv_pool,
+                                     float* rec_pool, const int32_t* slot_idx, int64_t n_slots, const void* norm_w,
+                                     float eps, void* out, int n, int Hk, int Hv, int dk, int dv, int K,
+                                     int conv_mode, void* workspace, size_t workspace_bytes, int dtype,
+                                     int32_t* err_flag, void* stream) {
+  return gdn::decode_layer_impl("gdn_decode_layer_rows", mixed_qkv, mixed_rs, z, z_rs, a, a_rs, b, b_rs, A_log,
+                                dt_bias, conv_w, conv_b, conv_pool, rec_pool, slot_idx, n_slots, norm_w, eps, out, n,
+                                Hk, Hv, dk, dv, K, conv_mode, workspace, workspace_bytes, dtype, err_flag, stream);
 }

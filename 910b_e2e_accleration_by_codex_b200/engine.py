@@ -24,6 +24,7 @@ from __future__ import annotations
 import os
 
 import torch
+import torch.nn as nn
 import torch.nn.functional as F
 
 from . import ops
@@ -35,6 +36,23 @@ ELEM_CONV = False
 
 # One captured decode graph per attention-length bucket of this many tokens (src/cb_engine.py:28).
 GRAPH_BUCKET = int(os.environ.get("CB_GRAPH_BUCKET", "512"))
+
+
+def fuse_linears(mods):
+    """One weight matrix for bias-free linears that read the same input: their weights stacked by rows
+    (padded with zero rows to a multiple of 8, so every slice of the product starts 16-byte aligned),
+    and each module's weight becomes a view into it, so no second copy stays in memory.  Returns
+    (W, the row count of each module)."""
+    ws = [m.weight.detach() for m in mods]
+    rows = sum(w.shape[0] for w in ws)
+    pad = (-rows) % 8
+    parts = ws + ([ws[0].new_zeros(pad, ws[0].shape[1])] if pad else [])
+    W = torch.cat(parts, 0)
+    off = 0
+    for m, w in zip(mods, ws):
+        m.weight = nn.Parameter(W[off:off + w.shape[0]], requires_grad=False)
+        off += w.shape[0]
+    return W, [w.shape[0] for w in ws]
 
 
 class CBEngine:
@@ -79,6 +97,22 @@ class CBEngine:
                     eps=float(getattr(gd.norm, "variance_epsilon", getattr(gd.norm, "eps", 1e-6))))
                 ws_bytes = max(ws_bytes, ops.decode_layer_workspace_bytes(n_slots, Hk, Hv, dk, dv, bf))
         self._ws = torch.zeros(max(ws_bytes, 256), dtype=torch.uint8, device=self.dev)  # decode tickets
+        # Decode runs one GEMM per group of projections that read the same input (the reference runs
+        # each projection separately): attention q/k/v, the GDN in_proj_qkv/z/b/a, the MLP gate/up.
+        # With 16-64 tokens a step these GEMMs are launch- and latency-bound, so fewer and wider ones
+        # save time at every TP degree.  The modules keep working (their weights are views).
+        self._fused = {}
+        for i, t in enumerate(cfg.layer_types):
+            layer = self.lm.layers[i]
+            if t == "full_attention":
+                at = layer.self_attn
+                W, sizes = fuse_linears([at.q_proj, at.k_proj, at.v_proj])
+            else:
+                gd = layer.linear_attn
+                W, sizes = fuse_linears([gd.in_proj_qkv, gd.in_proj_z, gd.in_proj_b, gd.in_proj_a])
+            mlp = layer.mlp
+            Wm, msz = fuse_linears([mlp.gate_proj, mlp.up_proj])
+            self._fused[i] = dict(W=W, sizes=sizes, Wm=Wm, inter=msz[0])
         hq_max = max([self.lm.layers[i].self_attn.q_proj.weight.shape[0] // (2 * self.lm.layers[i].self_attn.head_dim)
                       for i, t in enumerate(cfg.layer_types) if t == "full_attention"] or [1])
         hd_max = max([self.lm.layers[i].self_attn.head_dim
@@ -140,11 +174,14 @@ class CBEngine:
         n = h.shape[0]
         hd = at.head_dim
         kvh = self.kv_k[i].shape[1]
-        qg = at.q_proj(h).view(n, 1, -1, hd * 2)
+        f = self._fused[i]
+        nq, nk, _ = f["sizes"]
+        y = F.linear(h, f["W"])                       # [q | k | v] of one GEMM
+        qg = y[..., :nq].view(n, 1, -1, hd * 2)
         q, gate = torch.chunk(qg, 2, dim=-1)
         q = at.q_norm(q).transpose(1, 2)
-        k = at.k_norm(at.k_proj(h).view(n, 1, kvh, hd)).transpose(1, 2)
-        v = at.v_proj(h).view(n, 1, kvh, hd).transpose(1, 2)
+        k = at.k_norm(y[..., nq:nq + nk].view(n, 1, kvh, hd)).transpose(1, 2)
+        v = y[..., nq + nk:nq + 2 * nk].view(n, 1, kvh, hd).transpose(1, 2)
         q, k = self.M.apply_rotary_pos_emb(q, k, cos, sin)
         o = ops.attn_decode(q[:, :, 0], k[:, :, 0], v[:, :, 0], self.kv_k[i], self.kv_v[i], self._slot, pos32, Lmax,
                             at.scaling, gate=gate, workspace=self._attn_ws, err=self._err)
@@ -153,15 +190,23 @@ class CBEngine:
     def _gdn(self, gd, i, h):
         n = h.shape[0]
         p = self.gdn[i]
-        mixed = gd.in_proj_qkv(h).reshape(n, -1)
-        z = gd.in_proj_z(h).reshape(n, p["Hv"], p["dv"])
-        b = gd.in_proj_b(h).reshape(n, -1)
-        a = gd.in_proj_a(h).reshape(n, -1)
+        f = self._fused[i]
+        C, Z, Bn, An = f["sizes"]
+        y = F.linear(h.reshape(n, -1), f["W"])       # [qkv | z | b | a] of one GEMM; row-strided slices
+        mixed, z = y[:, :C], y[:, C:C + Z]
+        b, a = y[:, C + Z:C + Z + Bn], y[:, C + Z + Bn:C + Z + Bn + An]
         core = ops.decode_layer(mixed, z, a, b, p["A_log"], p["dt_bias"], p["conv_w"], p["conv_b"], self.conv[i],
                                 self.rec[i], self._slot, p["norm_w"], p["eps"], p["Hk"], p["Hv"], p["dk"], p["dv"],
                                 ops.GDN_CONV_ELEM if ELEM_CONV else ops.GDN_CONV_HF, workspace=self._ws,
                                 err=self._err)
         return gd.out_proj(core.reshape(n, 1, -1))
+
+    def _mlp(self, i, mlp, h):
+        """The layer's MLP (down(act(gate(h)) * up(h))) with gate and up from one GEMM."""
+        f = self._fused[i]
+        I = f["inter"]
+        y = F.linear(h, f["Wm"])
+        return mlp.down_proj(mlp.act_fn(y[..., :I]) * y[..., I:2 * I])
 
     def _core(self, Lmax):
         """One decode step for all N slots from the static buffers (capturable)."""
@@ -177,7 +222,7 @@ class CBEngine:
             else:
                 h = self._gdn(layer.linear_attn, i, h)
             x = x + h
-            x = x + layer.mlp(layer.post_attention_layernorm(x))
+            x = x + self._mlp(i, layer.mlp, layer.post_attention_layernorm(x))
         x = self.lm.norm(x)
         # next tokens and, as the last entry, the error flag after this step's kernels
         return torch.cat([self._greedy(x[:, 0]), self._err.to(torch.long)])

@@ -385,26 +385,41 @@ def decode_layer(mixed_qkv, z, a, b, A_log, dt_bias, conv_w, conv_b, conv_pool, 
     """The operator part of CBEngine._gdn (src/cb_engine.py:318-352) for n slots: conv update
     (conv_pool[slot_idx] in place) -> gates -> l2norm -> recurrence (rec_pool[slot_idx] in place)
     -> gated RMSNorm, as a prep kernel plus a persistent state kernel (d = 128) or one kernel
-    (d = 64).  ``workspace`` (see decode_layer_workspace) must be zero-filled before its first use.  mixed_qkv [n,C], z [n,Hv,dv], a/b [n,Hv],
-    A_log/dt_bias [Hv] fp32.  Returns out [n,Hv,dv]."""
+    (d = 64).  ``workspace`` (see decode_layer_workspace) must be zero-filled before its first use.
+    mixed_qkv [n,C], z [n,Hv,dv] (or [n,Hv*dv]), a/b [n,Hv], A_log/dt_bias [Hv] fp32.  Each of
+    mixed_qkv, z, a, b may be a row-strided view, e.g. column slices of one fused projection output
+    (gdn_decode_layer_rows).  Returns out [n,Hv,dv]."""
     _need_cuda(mixed_qkv, z, a, b, A_log, dt_bias, conv_w, conv_pool, rec_pool, slot_idx, norm_w)
     n, Cc = mixed_qkv.shape[0], mixed_qkv.shape[-1]
     mixed = mixed_qkv.reshape(n, Cc)
     if mixed.stride(1) != 1:
         mixed = mixed.contiguous()
-    if not z.is_contiguous() or z.data_ptr() % 16:  # the state kernel bulk-copies [dv] rows of z
-        z = z.clone(memory_format=torch.contiguous_format)
+
+    def rows(t, width):
+        """A [n, width] view of t with unit inner stride, or a contiguous copy."""
+        v = t.reshape(n, width) if t.is_contiguous() else (t if t.dim() == 2 else None)
+        if v is None or v.stride(1) != 1:
+            v = t.contiguous().reshape(n, width)
+        return v
+
+    z2, a2, b2 = rows(z, Hv * dv), rows(a, Hv), rows(b, Hv)
+    esz = z2.element_size()
+    if z2.data_ptr() % 16 or (z2.stride(0) * esz) % 16:  # the state kernel bulk-copies [dv] rows of z
+        z2 = z2.contiguous()
+        if z2.data_ptr() % 16:
+            z2 = z2.clone()
     K = conv_pool.shape[-1]
     if workspace is None:
         workspace = decode_layer_workspace(n, Hk, Hv, dk, dv, mixed.dtype, mixed.device)
     o = torch.empty(n, Hv, dv, dtype=mixed.dtype, device=mixed.device) if out is None else out
     w = conv_w.squeeze(1) if conv_w.dim() == 3 else conv_w
     lib = _lib.load()
-    _lib.check(lib.gdn_decode_layer(_p(mixed), mixed.stride(0), _p(z), _p(a), _p(b), _p(A_log), _p(dt_bias), _p(w),
-                                    _p(conv_b), _p(conv_pool), _p(rec_pool), _p(_i32(slot_idx)), rec_pool.shape[0],
-                                    _p(norm_w), float(eps), _p(o), n, Hk, Hv, dk, dv, K, conv_mode, _p(workspace),
-                                    workspace.numel(), _dtype_code(mixed), _p(err), _stream()),
-               "gdn_decode_layer")
+    _lib.check(lib.gdn_decode_layer_rows(_p(mixed), mixed.stride(0), _p(z2), z2.stride(0), _p(a2), a2.stride(0),
+                                         _p(b2), b2.stride(0), _p(A_log), _p(dt_bias), _p(w), _p(conv_b),
+                                         _p(conv_pool), _p(rec_pool), _p(_i32(slot_idx)), rec_pool.shape[0],
+                                         _p(norm_w), float(eps), _p(o), n, Hk, Hv, dk, dv, K, conv_mode,
+                                         _p(workspace), workspace.numel(), _dtype_code(mixed), _p(err), _stream()),
+               "gdn_decode_layer_rows")
     return o
 
 

@@ -87,6 +87,9 @@ def parse():
     ap.add_argument("--requests", type=int, default=0,
                     help="requests of the model leg (0: one per slot; configs 3/4 name 128 / 512)")
     ap.add_argument("--model-turns", type=int, default=6, help="most turns per request of the model leg")
+    ap.add_argument("--model-profile", action="store_true",
+                    help="after the model leg, profile graph-replayed decode steps (torch.profiler, device time "
+                         "per kernel) and report a per-category breakdown")
     ap.add_argument("--model-gen", type=int, default=512, help="greedy tokens per turn of the model leg")
     ap.add_argument("--model-allreduce", choices=["peer", "nccl"], default="peer",
                     help="TP decode sums: this library's peer-memory kernel or NCCL")
@@ -610,6 +613,56 @@ def tp_parity(world, rank, local):
     return res
 
 
+def decode_breakdown(eng, slots, steps=8, ctx=500):
+    """Device time per kernel category of graph-replayed decode steps (torch.profiler's CUPTI kernel
+    records; no replay, so it is safe on every rank of a TP run).  Every slot holds a ``ctx``-token
+    prompt; returns per-step milliseconds and kernel counts by category and the top kernels."""
+    from torch.profiler import ProfilerActivity, profile
+    V = MODEL_TEXT_CONFIG["vocab_size"]
+    g = torch.Generator().manual_seed(7)
+    all_slots = list(range(slots))
+    toks = eng.prefill_batch(all_slots, [torch.randint(0, V, (1, ctx), generator=g) for _ in all_slots])
+    for _ in range(3):
+        toks = eng.decode_step(all_slots, toks)
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(steps):
+            toks = eng.decode_step(all_slots, toks)
+        torch.cuda.synchronize()
+    for s_ in all_slots:
+        eng.free(s_)
+    cats = [("gdn decode layer (decode_prep + decode_state)", ("decode_prep_kernel", "decode_state_kernel")),
+            ("attention decode (attn_decode + combine)", ("attn_decode_kernel", "attn_combine_kernel")),
+            ("peer all-reduce (gdn_allreduce)", ("allreduce_bf16_kernel",)),
+            ("NCCL", ("nccl",)),
+            ("layer RMSNorm (gdn_rmsnorm)", ("rmsnorm_kernel",)),
+            ("GEMM (cuBLAS)", ("gemm", "nvjet", "xmma", "cublas", "cutlass", "gemv", "splitkreduce")),
+            ("elementwise / copy / reduce (torch)", ("elementwise", "vectorized", "reduce", "copy", "cat", "index",
+                                                     "fill", "softmax", "arange", "where", "unrolled"))]
+    by = {name: [0.0, 0] for name, _ in cats}
+    by["other"] = [0.0, 0]
+    rows = []
+    for e in prof.key_averages():
+        t = float(getattr(e, "device_time_total", 0.0) or 0.0)
+        if t <= 0 or e.count == 0:
+            continue
+        key = e.key
+        low = key.lower()
+        cat = next((name for name, pats in cats if any(p_ in low for p_ in pats)), "other")
+        by[cat][0] += t
+        by[cat][1] += e.count
+        rows.append((t, e.count, key))
+    rows.sort(reverse=True)
+    total = sum(v[0] for v in by.values())
+    return {"steps_profiled": steps, "context_tokens": ctx, "slots": slots,
+            "device_ms_per_step": total / 1e3 / steps,
+            "by_category_ms_per_step": {k: round(v[0] / 1e3 / steps, 4) for k, v in by.items() if v[1]},
+            "kernels_per_step": {k: v[1] / steps for k, v in by.items() if v[1]},
+            "top_kernels": [{"name": k[:90], "ms_per_step": round(t / 1e3 / steps, 4), "calls_per_step": c / steps}
+                            for t, c, k in rows[:12]],
+            "how": "torch.profiler CUDA kernel records of graph-replayed decode steps, device time summed per name"}
+
+
 def run_model(args, world, rank, local):
     """Model leg (configs 3/4): the random-init ~27B hybrid through the slot engine, serving the
     synthetic multi-turn request workload with continuous batching (serve.run_requests)."""
@@ -663,6 +716,7 @@ def run_model(args, world, rank, local):
     st = serve.run_requests(eng, reqs, gen_tokens=args.model_gen, on_step=on_step)
     torch.cuda.synchronize()
     barrier(world)
+    breakdown = decode_breakdown(eng, slots) if args.model_profile else None
     eng.check_errors()
     if world > 1:
         eng.close()                              # graphs and peer buffers go before the process group
@@ -707,6 +761,8 @@ def run_model(args, world, rank, local):
            "lm_head": "vocabulary-parallel" if world > 1 else "full", "build_s": build_s}
     if parity is not None:
         out["tp_parity"] = parity
+    if breakdown is not None:
+        out["decode_breakdown"] = breakdown
     return out
 
 

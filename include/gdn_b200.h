@@ -157,6 +157,24 @@ GDN_API int gdn_decode_layer(const void* mixed_qkv, int64_t mixed_rs, const void
                      void* workspace, size_t workspace_bytes, int dtype, int32_t* err_flag,
                      void* stream);
 
+/* gdn_decode_layer with explicit row strides (elements between the rows of
+ * consecutive slot entries) for z (z_rs >= Hv*dv), a (a_rs >= Hv) and b
+ * (b_rs >= Hv), so that they can be column slices of one fused projection
+ * output [n, C + Hv*dv + 2*Hv] (the reference computes them with separate
+ * in_proj_z / in_proj_a / in_proj_b GEMMs, src/cb_engine.py:320-323).  z's
+ * rows move by 16-byte bulk copies: z and z_rs * element size must be
+ * 16-byte aligned.  Everything else as gdn_decode_layer, which is this call
+ * with z_rs = Hv*dv and a_rs = b_rs = Hv.
+ */
+GDN_API int gdn_decode_layer_rows(const void* mixed_qkv, int64_t mixed_rs, const void* z, int64_t z_rs,
+                                  const void* a, int64_t a_rs, const void* b, int64_t b_rs,
+                                  const float* A_log, const float* dt_bias, const void* conv_w,
+                                  const void* conv_b, void* conv_pool, float* rec_pool,
+                                  const int32_t* slot_idx, int64_t n_slots, const void* norm_w, float eps,
+                                  void* out, int n, int Hk, int Hv, int dk, int dv, int K, int conv_mode,
+                                  void* workspace, size_t workspace_bytes, int dtype, int32_t* err_flag,
+                                  void* stream);
+
 /* ---------------------------------------------------------------------------
  * gdn_decode_layer for callers that cannot allocate device memory.  This
  * entry point has no counterpart in the reference; the reference never

@@ -624,3 +624,38 @@ def test_chunk_tc_full_config1_vs_oracle_and_fp32_path(ops):
                                           beta[s:e].numpy()[None], 64, init[b].numpy()[None], True, True, "bf16")
         assert bf16_ok(N(o_tc[s:e]), ro[0])
         assert np.abs(N(pool_tc[15 - b]) - rs[0]).max() < 2e-2
+
+
+@pytest.mark.parametrize("d,Hk,Hv", [(128, 4, 12), (64, 2, 8)])
+def test_decode_layer_row_strided_inputs_bit_exact(ops, d, Hk, Hv):
+    """mixed_qkv, z, b and a as column slices of one fused projection output [n, C + Hv d + 2 Hv]
+    (gdn_decode_layer_rows, what the engine's fused decode GEMM produces) give exactly what the same
+    values as separate contiguous tensors give, outputs and both pools."""
+    g = torch.Generator().manual_seed(11)
+    n, S, K = 5, 9, 4
+    C = 2 * Hk * d + Hv * d
+    tot = C + Hv * d + 2 * Hv
+    tot += (-tot) % 8
+    bf = torch.bfloat16
+    y = torch.randn(n, tot, generator=g).to(bf).to(DEV)
+    mixed, z = y[:, :C], y[:, C:C + Hv * d]
+    b, a = y[:, C + Hv * d:C + Hv * d + Hv], y[:, C + Hv * d + Hv:C + Hv * d + 2 * Hv]
+    A_log = torch.log(torch.empty(Hv).uniform_(1, 16, generator=g)).to(DEV)
+    dt_bias = (torch.rand(Hv, generator=g) * 2 - 1).to(DEV)
+    cw = (torch.rand(C, K, generator=g) - 0.5).to(bf).to(DEV)
+    nw = (1 + 0.1 * torch.randn(d, generator=g)).to(bf).to(DEV)
+    cpool = torch.randn(S, C, K, generator=g).to(bf).to(DEV)
+    rpool = (torch.randn(S, Hv, d, d, generator=g) * 0.05).to(DEV)
+    slot = torch.randperm(S, generator=g)[:n].to(torch.int32).to(DEV)
+    outs = []
+    for strided in (True, False):
+        cp, rp = cpool.clone(), rpool.clone()
+        args = (mixed, z, a, b) if strided else tuple(t.contiguous() for t in (mixed, z, a, b))
+        if strided:
+            assert not args[1].is_contiguous() and not args[2].is_contiguous()
+        o = ops.decode_layer(*args, A_log, dt_bias, cw, None, cp, rp, slot, nw, 1e-6, Hk, Hv, d, d,
+                             ops.GDN_CONV_HF)
+        torch.cuda.synchronize()
+        outs.append((o, cp, rp))
+    for x, y_ in zip(outs[0], outs[1]):
+        assert torch.equal(x, y_)
