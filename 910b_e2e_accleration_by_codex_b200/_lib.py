@@ -57,6 +57,11 @@ SIGNATURES = {
     "gdn_ar_ipc_open": (_i32, [_vp, C.POINTER(_vp)]),
     "gdn_ar_ipc_close": (_i32, [_vp]),
     "gdn_allreduce": (_i32, [_vp, _vp, _sz, _i32, _i32, _i32, _vp, _sz, C.c_uint32, _vp, _vp]),
+    "gdn_linear": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _i32, _i32, _i32, _i32, _i32, _vp, _vp]),
+    "gdn_linear_plan": (_i32, [_i32, _i32, _i32, _i32, _i32, _vp]),
+    "gdn_linear_ar_buffer_bytes": (_sz, [_i32, _i32, _i32, _i32]),
+    "gdn_linear_allreduce": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _i32, _i32, _i32, _i32, _i32, _i32, _vp,
+                                    _i32, _i32, C.c_uint32, _vp, _i32, _vp]),
 }
 GDN_IPC_HANDLE_BYTES = 64
 

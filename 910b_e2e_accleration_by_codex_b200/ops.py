@@ -426,3 +426,41 @@ def decode_layer(mixed_qkv, z, a, b, A_log, dt_bias, conv_w, conv_b, conv_pool, 
 def l2_scale(dk: int) -> float:
     """The q scale the reference applies after l2norm (1/sqrt(dk))."""
     return 1.0 / math.sqrt(dk)
+
+
+# ============================================================================ f1: decode projections
+def _linear_operands(x, weight):
+    _need_cuda(x, weight)
+    if x.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16:
+        raise TypeError("linear: bf16 x and weight")
+    k = x.shape[-1]
+    x2 = x.reshape(-1, k)
+    if x2.stride(-1) != 1 or x2.stride(0) % 8 or x2.data_ptr() % 16:
+        x2 = x2.contiguous()
+    w = weight if weight.stride(-1) == 1 and weight.stride(0) % 8 == 0 and weight.data_ptr() % 16 == 0 \
+        else weight.contiguous()
+    return x2, w
+
+
+def linear(x: torch.Tensor, weight: torch.Tensor, out: torch.Tensor | None = None, splits: int = 0,
+           err: torch.Tensor | None = None) -> torch.Tensor:
+    """F.linear(x, weight) for a bias-free projection of a decode step (src/cb_engine.py:295-355) on
+    the tensor cores (gdn_linear): x [..., k] bf16 with at most 256 rows, weight [n_out, k] bf16;
+    fp32 accumulation, one bf16 rounding, deterministic.  ``splits`` forces the K split (0: the
+    library picks)."""
+    x2, w = _linear_operands(x, weight)
+    n, n_out, k = x2.shape[0], w.shape[0], x2.shape[1]
+    y = torch.empty(n, n_out, dtype=x.dtype, device=x.device) if out is None else out.view(-1, n_out)
+    lib = _lib.load()
+    _lib.check(lib.gdn_linear(_p(x2), x2.stride(0), _p(w), w.stride(0), _p(y), y.stride(0), n, n_out, k, int(splits),
+                              GDN_BF16, _p(err), _stream()), "gdn_linear")
+    return y.view(*x.shape[:-1], n_out)
+
+
+def linear_plan(n, n_out, k, splits=0, world=1):
+    """The launch gdn_linear (world 1) / gdn_linear_allreduce (world > 1) makes for this shape:
+    dict(splits, stages, smem, tiles, kblocks)."""
+    import ctypes
+    out = (ctypes.c_int32 * 5)()
+    _lib.check(_lib.load().gdn_linear_plan(n, n_out, k, splits, world, out), "gdn_linear_plan")
+    return dict(zip(("splits", "stages", "smem", "tiles", "kblocks"), list(out)))

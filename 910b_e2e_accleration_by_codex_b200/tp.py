@@ -25,28 +25,21 @@ import torch
 import torch.distributed as dist
 import torch.nn as nn
 
-from . import _lib
+from . import _lib, ops
 from .engine import CBEngine
 
 
-class PeerAllReduce:
-    """In-place sum over the ranks of the process group (one process per GPU, one node) by
-    gdn_allreduce over IPC-mapped peer buffers, for bf16 outputs of up to ``max_elems`` elements.
-    Collective: every rank constructs it, calls it on tensors of the same sizes in the same order
-    (CUDA-graph capture included) and closes it.  Each rank's result is the fp32 sum in rank order
-    rounded once to bf16, identical on all ranks.  If a rank does not arrive within ``spin_limit``
-    polls the others set ``err`` to 3 and leave their tensor as it was; the instance is then out of
-    step and must be closed."""
+class _PeerBuffers:
+    """One device buffer per rank (gdn_ar_alloc, zero-filled) whose CUDA IPC handle every other rank
+    opens, so each rank holds plain pointers to all buffers of the node.  Collective: every rank
+    constructs it and closes it."""
 
-    def __init__(self, max_elems, device, spin_limit=0):
+    def __init__(self, nbytes, device, what):
         lib = _lib.load()
         self.lib = lib
         self.rank, self.world = dist.get_rank(), dist.get_world_size()
-        self.max_elems = int(max_elems)
-        self.spin_limit = int(spin_limit)
-        nbytes = lib.gdn_ar_buffer_bytes(self.world, self.max_elems, _lib.GDN_BF16)
         if nbytes == 0:
-            raise RuntimeError(f"PeerAllReduce: world {self.world} not supported (1..8 ranks)")
+            raise RuntimeError(f"{what}: world {self.world} or the sizes are not supported")
         own = C.c_void_p()
         _lib.check(lib.gdn_ar_alloc(nbytes, C.byref(own)), "gdn_ar_alloc")
         handle = C.create_string_buffer(_lib.GDN_IPC_HANDLE_BYTES)
@@ -67,6 +60,35 @@ class PeerAllReduce:
         self.err = torch.zeros(1, dtype=torch.int32, device=device)
         self.closed = False
 
+    def close(self):
+        """Collective: after every rank's last call, unmap the peers' buffers and free this one."""
+        if self.closed:
+            return
+        self.closed = True
+        torch.cuda.synchronize()
+        dist.barrier()
+        for r, ptr in enumerate(self._ptrs):
+            if r != self.rank:
+                _lib.check(self.lib.gdn_ar_ipc_close(ptr), "gdn_ar_ipc_close")
+        dist.barrier()  # no rank writes into this buffer any more
+        _lib.check(self.lib.gdn_ar_free(self._own), "gdn_ar_free")
+
+
+class PeerAllReduce(_PeerBuffers):
+    """In-place sum over the ranks of the process group (one process per GPU, one node) by
+    gdn_allreduce over IPC-mapped peer buffers, for bf16 outputs of up to ``max_elems`` elements.
+    Collective: every rank constructs it, calls it on tensors of the same sizes in the same order
+    (CUDA-graph capture included) and closes it.  Each rank's result is the fp32 sum in rank order
+    rounded once to bf16, identical on all ranks.  If a rank does not arrive within ``spin_limit``
+    polls the others set ``err`` to 3 and leave their tensor as it was; the instance is then out of
+    step and must be closed."""
+
+    def __init__(self, max_elems, device, spin_limit=0):
+        self.max_elems = int(max_elems)
+        self.spin_limit = int(spin_limit)
+        nbytes = _lib.load().gdn_ar_buffer_bytes(dist.get_world_size(), self.max_elems, _lib.GDN_BF16)
+        super().__init__(nbytes, device, "PeerAllReduce")
+
     def applies(self, y):
         """Whether ``y`` goes through this kernel (the same answer on every rank for the same shape)."""
         return (not self.closed and y.dtype == torch.bfloat16 and y.numel() <= self.max_elems
@@ -85,18 +107,40 @@ class PeerAllReduce:
                    "gdn_allreduce")
         return y
 
-    def close(self):
-        """Collective: after every rank's last call, unmap the peers' buffers and free this one."""
-        if self.closed:
-            return
-        self.closed = True
-        torch.cuda.synchronize()
-        dist.barrier()
-        for r, ptr in enumerate(self._ptrs):
-            if r != self.rank:
-                _lib.check(self.lib.gdn_ar_ipc_close(ptr), "gdn_ar_ipc_close")
-        dist.barrier()  # no rank writes into this buffer any more
-        _lib.check(self.lib.gdn_ar_free(self._own), "gdn_ar_free")
+
+class PeerLinearAllReduce(_PeerBuffers):
+    """A row-parallel projection and its sum over the ranks in one kernel (gdn_linear_allreduce):
+    ``self(x, weight)`` = sum over ranks of x_r weight_r^T, for up to ``max_rows`` tokens and
+    ``max_out`` output features (bf16).  Each rank's product is rounded to bf16, as the unfused
+    GEMM output, and the ranks' partials are summed in rank order in fp32 and rounded once, so all
+    ranks get identical results.  Collective like PeerAllReduce (same calls, same shapes, same
+    order on every rank; a rank that does not arrive makes the others set ``err`` to 3)."""
+
+    def __init__(self, max_rows, max_out, device, spin_limit=0):
+        self.max_rows, self.max_out = int(max_rows), int(max_out)
+        self.spin_limit = int(spin_limit)
+        nbytes = _lib.load().gdn_linear_ar_buffer_bytes(dist.get_world_size(), self.max_rows, self.max_out,
+                                                        _lib.GDN_BF16)
+        super().__init__(nbytes, device, "PeerLinearAllReduce")
+
+    def applies(self, x, weight):
+        """Whether this projection goes through the fused kernel (depends only on shapes and dtypes,
+        so every rank answers alike)."""
+        k = x.shape[-1]
+        return (not self.closed and x.is_cuda and x.dtype == torch.bfloat16 and weight.dtype == torch.bfloat16
+                and x.numel() // max(k, 1) <= self.max_rows and weight.shape[0] <= self.max_out
+                and weight.shape[0] % 8 == 0 and k % 8 == 0 and weight.shape[1] == k)
+
+    def __call__(self, x, weight, splits=0):
+        x2, w = ops._linear_operands(x, weight)
+        n, n_out, k = x2.shape[0], w.shape[0], x2.shape[1]
+        y = torch.empty(n, n_out, dtype=x.dtype, device=x.device)
+        _lib.check(self.lib.gdn_linear_allreduce(x2.data_ptr(), x2.stride(0), w.data_ptr(), w.stride(0), y.data_ptr(),
+                                                 n_out, n, n_out, k, int(splits), self.rank, self.world, self._table,
+                                                 self.max_rows, self.max_out, self.spin_limit, self.err.data_ptr(),
+                                                 _lib.GDN_BF16, torch.cuda.current_stream().cuda_stream),
+                   "gdn_linear_allreduce")
+        return y.view(*x.shape[:-1], n_out)
 
 
 _PEER_AR = None
@@ -119,17 +163,41 @@ def disable_peer_allreduce():
         _PEER_AR = None
 
 
+_PEER_LINEAR = None
+
+
+def enable_peer_linear(max_rows, max_out, device, spin_limit=0):
+    """Collective: run AllReduceLinear's projections of up to ``max_rows`` tokens and ``max_out``
+    outputs as one fused kernel (PeerLinearAllReduce, returned)."""
+    global _PEER_LINEAR
+    disable_peer_linear()
+    _PEER_LINEAR = PeerLinearAllReduce(max_rows, max_out, device, spin_limit)
+    return _PEER_LINEAR
+
+
+def disable_peer_linear():
+    """Collective: close the PeerLinearAllReduce in use, if any."""
+    global _PEER_LINEAR
+    if _PEER_LINEAR is not None:
+        _PEER_LINEAR.close()
+        _PEER_LINEAR = None
+
+
 class AllReduceLinear(nn.Module):
     """A row-parallel projection: this rank holds a block of the input columns, so its product is
     a partial sum; the full output is the sum of the partials over all ranks (the same on every
-    rank afterwards).  Decode-sized outputs are summed by the peer-memory kernel when one is
-    enabled, everything else by NCCL (src/cb_tp.py:25-35 is the reference's version)."""
+    rank afterwards).  Decode-sized inputs go through the fused projection + peer sum kernel when
+    one is enabled (else the peer-memory all-reduce after a cuBLAS GEMM, when enabled), everything
+    else through F.linear + NCCL (src/cb_tp.py:25-35 is the reference's version)."""
 
     def __init__(self, lin):
         super().__init__()
         self.lin = lin
 
     def forward(self, x):
+        fused = _PEER_LINEAR
+        if fused is not None and self.lin.bias is None and fused.applies(x, self.lin.weight):
+            return fused(x, self.lin.weight)
         partial = self.lin(x)
         reducer = _PEER_AR
         if reducer is None or not reducer.applies(partial):
@@ -327,29 +395,44 @@ def init_tp(rank, world, backend="nccl", master_port="29561", timeout_s=120):
 
 
 class TPEngine(CBEngine):
-    """CBEngine on sharded weights (src/cb_tp.py:117-285).  With ``peer_allreduce`` (default) the
-    decode steps' row-parallel sums ([slots, hidden] bf16) go through PeerAllReduce and prefill's
-    larger ones through NCCL; decode graphs capture whichever runs, and every rank captures the same
-    sequence of graphs.  ``close()`` (collective) releases the graphs and the peer buffers."""
+    """CBEngine on sharded weights (src/cb_tp.py:117-285).  With ``fused_linear`` the decode
+    steps' row-parallel projections run as one kernel each that also sums over the ranks
+    (PeerLinearAllReduce); with ``peer_allreduce`` (default) decode-sized sums the fused kernel does
+    not take go through PeerAllReduce after a cuBLAS GEMM; prefill's larger ones through F.linear +
+    NCCL.
+    Decode graphs capture whichever runs, and every rank captures the same sequence of graphs.
+    ``close()`` (collective) releases the graphs and the peer buffers."""
 
-    def __init__(self, model, n_slots, t_max, device, tp, graph_decode=False, peer_allreduce=True):
-        self.peer_ar = None
-        if peer_allreduce and tp > 1:
+    def __init__(self, model, n_slots, t_max, device, tp, graph_decode=False, peer_allreduce=True,
+                 fused_linear=False):
+        self.peer_ar = self.peer_linear = None
+        if tp > 1:
             hidden = model.config.text_config.hidden_size
-            self.peer_ar = enable_peer_allreduce(n_slots * hidden, device)
+            if peer_allreduce:
+                self.peer_ar = enable_peer_allreduce(n_slots * hidden, device)
+            if fused_linear:
+                self.peer_linear = enable_peer_linear(n_slots, hidden, device)
         super().__init__(model, n_slots, t_max, device, graph_decode=graph_decode, tp=tp)
 
     def check_errors(self):
-        """Raise if a kernel of the engine reported an error or a peer all-reduce timed out (a rank
+        """Raise if a kernel of the engine reported an error or a peer exchange timed out (a rank
         did not arrive)."""
         super().check_errors()
-        if self.peer_ar is not None and int(self.peer_ar.err.item()) != 0:
-            raise RuntimeError(f"peer all-reduce error {int(self.peer_ar.err.item())} (a rank did not arrive)")
+        for what, inst in (("peer all-reduce", self.peer_ar), ("fused projection + all-reduce", self.peer_linear)):
+            if inst is not None and int(inst.err.item()) != 0:
+                raise RuntimeError(f"{what} error {int(inst.err.item())} (a rank did not arrive)")
 
     def close(self):
-        """Collective: release the decode graphs and the peer all-reduce buffers."""
+        """Collective: release the decode graphs and the peer buffers."""
         self._graphs.clear()
         self._graph_out.clear()
+        if self.peer_linear is not None:
+            torch.cuda.synchronize()
+            if _PEER_LINEAR is self.peer_linear:
+                disable_peer_linear()
+            else:
+                self.peer_linear.close()
+            self.peer_linear = None
         if self.peer_ar is not None:
             torch.cuda.synchronize()
             if _PEER_AR is self.peer_ar:

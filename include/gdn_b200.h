@@ -310,6 +310,54 @@ GDN_API int gdn_ar_ipc_close(void* ptr);
 GDN_API int gdn_allreduce(const void* x, void* y, size_t n, int dtype, int rank, int world, void* const* bufs,
                           size_t max_elems, uint32_t spin_limit, int32_t* err_flag, void* stream);
 
+/* ---------------------------------------------------------------------------
+ * f1. Decode projections on the tensor cores, and the row-parallel projection
+ * fused with its all-reduce.
+ *
+ * gdn_linear: y[n, n_out] = x[n, k] W[n_out, k]^T (bf16 in, fp32 accumulation,
+ * bf16 out), the F.linear of a projection of a decode step
+ * (src/cb_engine.py:295-355; nn.Linear without bias), for n = 1..256 tokens.
+ * W is streamed once through TMA as the M = 128 operand of tcgen05.mma; the
+ * K range of each 128-feature tile is split over the CTAs of a thread-block
+ * cluster (splits = 0: chosen from the shape; 1..8: forced) and the partial
+ * accumulators are summed through distributed shared memory in split order,
+ * so results are deterministic.  No workspace.  Row strides in elements
+ * (multiples of 8); x, W, y 16-byte aligned; n_out, k multiples of 8.  A
+ * bounded wait that runs out sets *err_flag = 2 (err_flag may be NULL).
+ *
+ * gdn_linear_allreduce: y = sum over ranks of x_r W_r^T, replacing
+ * AllReduceLinear.forward (src/cb_tp.py:25-35: F.linear then dist.all_reduce)
+ * in one kernel.  Each rank's product is rounded to bf16 (as the unfused GEMM
+ * output) and every 16-feature segment is sent with plain stores to every
+ * rank's exchange buffer as soon as its split reduction is done; y is the
+ * fp32 sum of the ranks' bf16 partials in rank order, rounded once (identical
+ * on every rank).  Buffers: gdn_linear_ar_buffer_bytes(world, max_rows,
+ * max_out) bytes per rank from gdn_ar_alloc, shared through gdn_ar_ipc_handle /
+ * gdn_ar_ipc_open as for gdn_allreduce; every call on them passes the same
+ * max_rows >= n and max_out >= n_out (<= 65536).  Every rank makes the same
+ * calls with the same shapes and splits; a rank that does not arrive within
+ * spin_limit polls (0: 2^22) makes the others set *err_flag = 3 and leave y
+ * unwritten (recreate the buffers).  world = 1 is gdn_linear.  No multicast
+ * memory and no bulk/TMA reads of peer memory.
+ *
+ * With world > 1 every cluster of the launch must be resident at once (a CTA
+ * waiting for the other ranks holds its SMs): the split count is lowered until
+ * the device holds all tiles' clusters together, else GDN_ERR_SHAPE.
+ *
+ * gdn_linear_plan fills out[5] (five int32) with the launch gdn_linear (world
+ * = 1) or gdn_linear_allreduce (world > 1) makes: splits (CTAs per cluster),
+ * pipeline stages, dynamic shared memory bytes per CTA, 128-feature tiles
+ * (clusters), 64-wide k-blocks.
+ */
+GDN_API int gdn_linear(const void* x, int64_t x_rs, const void* w, int64_t w_rs, void* y, int64_t y_rs, int n,
+                       int n_out, int k, int splits, int dtype, int32_t* err_flag, void* stream);
+GDN_API int gdn_linear_plan(int n, int n_out, int k, int splits, int world, int32_t* out);
+GDN_API size_t gdn_linear_ar_buffer_bytes(int world, int max_rows, int max_out, int dtype);
+GDN_API int gdn_linear_allreduce(const void* x, int64_t x_rs, const void* w, int64_t w_rs, void* y, int64_t y_rs,
+                                 int n, int n_out, int k, int splits, int rank, int world, void* const* bufs,
+                                 int max_rows, int max_out, uint32_t spin_limit, int32_t* err_flag, int dtype,
+                                 void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,153 @@
+"""The row-parallel projection fused with its sum over ranks (gdn_linear_allreduce,
+tp.PeerLinearAllReduce) on 2 GPUs (4 when four are visible), one process each.
+
+Each rank's product is rounded to bf16 as the unfused GEMM output would be, and the ranks'
+partials are summed in rank order in fp32 and rounded once.  gdn_linear with the same split count
+computes exactly that per-rank partial, so every rank checks its result BIT FOR BIT against
+bf16(sum over r of fp32(gdn_linear(x_r, W_r)))
+(the partials gathered with NCCL), and that all ranks hold identical results.  Shapes change from
+call to call (the per-segment epochs and the double-buffered slots must stay in step; outputs
+narrower than the buffers; 1-128 tokens), the calls are also captured in a CUDA graph and replayed
+with fresh inputs, and the result is compared with F.linear + NCCL all-reduce within bf16
+tolerance.  A second instance with a short spin limit checks the failure path: only rank 0 calls,
+its wait runs out, it reports error 3 and leaves y unwritten, while the other ranks wait in a host
+barrier (buffers mapped, no kernel in flight).  Skipped when fewer than two GPUs are visible.
+"""
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+HIDDEN = 5120
+MAX_ROWS = 128
+# (tokens, output features, local k): decode shapes of TP 2-8 and odd ones
+CASES = [(32, 5120, 3072), (32, 5120, 8704), (7, 1040, 1000), (128, 5120, 768), (16, 5120, 2176), (1, 8, 64),
+         (64, 2056, 4352)]
+
+
+def inp(rank, case, n, n_out, k):
+    g = torch.Generator(device="cpu").manual_seed(1000 * case + rank)
+    x = torch.randn(n, k, generator=g).to(torch.bfloat16)
+    w = (torch.randn(n_out, k, generator=g) / k ** 0.5).to(torch.bfloat16)
+    return x, w
+
+
+def _rank(rank, world, port, q):
+    import sys
+    sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+    from conftest import pkg
+    os.environ["LOCAL_RANK"] = str(rank)
+    tp = pkg("tp")
+    ops = pkg("ops")
+    tp.init_tp(rank, world, "nccl", str(port), timeout_s=60)
+    import torch.distributed as dist
+    dev = torch.device("cuda", rank)
+    out = {}
+
+    def expected(x, w):
+        S = ops.linear_plan(x.shape[0], w.shape[0], x.shape[1], world=world)["splits"]
+        part = ops.linear(x, w, splits=S)             # this rank's bf16 partial, same split count
+        parts = [torch.empty_like(part) for _ in range(world)]
+        dist.all_gather(parts, part)
+        acc = torch.zeros(part.shape, dtype=torch.float32, device=dev)
+        for p in parts:
+            acc += p.float()
+        return acc.to(torch.bfloat16)
+
+    def same_on_all(y):
+        ys = [torch.empty_like(y) for _ in range(world)]
+        dist.all_gather(ys, y)
+        return all(torch.equal(ys[0], t) for t in ys)
+
+    try:
+        fl = tp.PeerLinearAllReduce(MAX_ROWS, HIDDEN, dev)
+        ok, same, close = True, True, True
+        for rep in range(2):
+            for case, (n, n_out, k) in enumerate(CASES):
+                x, w = (t.to(dev) for t in inp(rank, 10 * rep + case, n, n_out, k))
+                assert fl.applies(x, w)
+                y = fl(x, w)
+                ok &= torch.equal(y, expected(x, w))
+                same &= same_on_all(y)
+                if case == 0:
+                    z = torch.nn.functional.linear(x, w)
+                    dist.all_reduce(z)
+                    mag = (x.float().abs() @ w.float().abs().t())
+                    mag_all = mag.clone()
+                    dist.all_reduce(mag_all)
+                    close &= bool(((y.float() - z.float()).abs() <= 2 ** -6 * mag_all + 1e-2).all())
+        torch.cuda.synchronize()
+        out["eager"], out["same"], out["nccl_close"] = ok, same, close
+        # CUDA graph: three fused projections captured, replayed with fresh inputs
+        shapes = [CASES[0], CASES[3], CASES[1]]
+        xs = [torch.zeros(n, k, dtype=torch.bfloat16, device=dev) for n, _, k in shapes]
+        ws = [torch.zeros(n_out, k, dtype=torch.bfloat16, device=dev) for _, n_out, k in shapes]
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(graph, stream=s):
+                ys = [fl(x, w) for x, w in zip(xs, ws)]
+        torch.cuda.current_stream().wait_stream(s)
+        ok = True
+        for rep in range(3):
+            for i, (n, n_out, k) in enumerate(shapes):
+                x, w = inp(rank, 500 + 10 * rep + i, n, n_out, k)
+                xs[i].copy_(x)
+                ws[i].copy_(w)
+            graph.replay()
+            torch.cuda.synchronize()
+            for i in range(len(shapes)):
+                ok &= torch.equal(ys[i], expected(xs[i], ws[i]))
+        out["graph"] = ok
+        del graph
+        out["err"] = int(fl.err.item())
+        out["applies_big"] = fl.applies(torch.zeros(MAX_ROWS + 1, 64, dtype=torch.bfloat16, device=dev),
+                                        torch.zeros(64, 64, dtype=torch.bfloat16, device=dev))
+        fl.close()
+        # failure path: rank 0 alone calls; its bounded waits run out
+        fl2 = tp.PeerLinearAllReduce(16, 1024, dev, spin_limit=20000)
+        if rank == 0:
+            x, w = (t.to(dev) for t in inp(0, 7, 16, 1024, 512))
+            y = fl2(x, w)
+            torch.cuda.synchronize()
+            out["timeout_err"] = int(fl2.err.item())
+        dist.barrier()                       # the other ranks wait here while rank 0's kernel runs
+        fl2.close()
+        q.put((rank, out))
+    finally:
+        dist.destroy_process_group()
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def test_fused_linear_allreduce_multi_gpu():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    world = 4 if torch.cuda.device_count() >= 4 else 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    codes = [p.exitcode for p in procs]
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    assert codes == [0] * world, codes
+    res = dict(q.get(timeout=5) for _ in range(world))
+    for r in range(world):
+        assert res[r]["eager"] and res[r]["same"] and res[r]["graph"] and res[r]["nccl_close"], res[r]
+        assert res[r]["err"] == 0 and not res[r]["applies_big"], res[r]
+    assert res[0]["timeout_err"] == 3, res[0]
