@@ -4,7 +4,8 @@ Two spawned ranks shard a small seeded Qwen3.5 (2 GDN k heads / 4 v heads, 4 att
 over 1 KV head, so TP 2 also exercises the KV-head replication) with tp.shard_model, run
 TPEngine over two prompts and four teacher-forced decode steps, eagerly (rank 0 writes the logits
 of every step) and with CUDA-graph decode (the NCCL all-reduces captured in the graphs; its tokens
-must equal the eager argmax bit for bit).  The parent runs CBEngine on one GPU with the same model
+must equal the eager argmax bit for bit), once with the row-parallel projections followed by the
+peer all-reduce and once with them fused into one kernel each (gdn_linear_allreduce).  The parent runs CBEngine on one GPU with the same model
 and feed and compares the logits: the all-reduce changes the summation order, so the check is
 bf16 tolerance (2e-2 relative to the logit scale), not bits.
 Skipped when fewer than two GPUs are visible.
@@ -90,6 +91,10 @@ def _rank(rank, world, port, out_path):
         # graph replay (all-reduces inside the graph) == eager, bit for bit on this rank
         eager_toks = [lg.argmax(-1).tolist() for lg in logits[1:]]
         assert graph_toks == eager_toks, (graph_toks, eager_toks)
+        # the row-parallel projections fused with their sum over ranks (gdn_linear_allreduce)
+        flogits = run(tp.TPEngine, model, dev, False, tp=world, fused_linear=True)
+        fgraph_toks = run(tp.TPEngine, model, dev, True, tp=world, fused_linear=True)
+        assert fgraph_toks == [lg.argmax(-1).tolist() for lg in flogits[1:]]
         # the LM head split by vocabulary (cross-rank packed argmax, captured in the graphs): the same
         # tokens wherever the eager logits' top two are not a near-tie
         vmodel = build_model(dev)
@@ -102,6 +107,7 @@ def _rank(rank, world, port, out_path):
                     assert tok == int(lg[row].argmax()), (row, tok, int(lg[row].argmax()))
         if rank == 0:
             np.savez(out_path, *logits)
+            np.savez(out_path + ".fused.npz", *flogits)
     finally:
         import torch.distributed as dist
         dist.destroy_process_group()
@@ -131,9 +137,13 @@ def test_tp2_engine_matches_single_gpu():
                 p.kill()
         assert codes == [0, 0], codes
         tp_logits = [v for _, v in sorted(np.load(out_path).items(), key=lambda kv: int(kv[0].split("_")[1]))]
+        fused_logits = [v for _, v in sorted(np.load(out_path + ".fused.npz").items(),
+                                             key=lambda kv: int(kv[0].split("_")[1]))]
     eng = pkg("engine")
     ref = run(eng.CBEngine, build_model(torch.device("cuda", 0)), torch.device("cuda", 0), False)
-    assert len(ref) == len(tp_logits) == 5
-    for step, (a, b) in enumerate(zip(tp_logits, ref)):
+    assert len(ref) == len(tp_logits) == len(fused_logits) == 5
+    for step, (a, f, b) in enumerate(zip(tp_logits, fused_logits, ref)):
         err = float(np.abs(a - b).max())
         assert err <= 2e-2 * float(np.abs(b).max()) + 2e-2, (step, err)
+        ferr = float(np.abs(f - b).max())
+        assert ferr <= 2e-2 * float(np.abs(b).max()) + 2e-2, (step, ferr)
