@@ -62,6 +62,11 @@ SIGNATURES = {
     "gdn_linear_ar_buffer_bytes": (_sz, [_i32, _i32, _i32, _i32]),
     "gdn_linear_allreduce": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _i32, _i32, _i32, _i32, _i32, _i32, _vp,
                                     _i32, _i32, C.c_uint32, _vp, _i32, _vp]),
+    "gdn_linear_push": (_i32, [_vp, _i64, _vp, _i64, _i32, _i32, _i32, _i32, _i32, _i32, _vp, _i32, _i32, _vp,
+                               _i32, _vp]),
+    "gdn_pull_add_rmsnorm": (_i32, [_vp, _i64, _vp, _vp, _i64, _i64, _i32, _f32, _i32, _i32, _vp, _i32, _i32,
+                                    C.c_uint32, _vp, _i32, _vp]),
+    "gdn_add_rmsnorm": (_i32, [_vp, _i64, _vp, _i64, _vp, _vp, _i64, _i64, _i32, _f32, _i32, _vp]),
 }
 GDN_IPC_HANDLE_BYTES = 64
 

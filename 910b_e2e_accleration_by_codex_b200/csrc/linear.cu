@@ -32,6 +32,12 @@
 //   [kDataOff, ...)          data[2][world][max_out / 8][max_rows] 16-byte vectors (8 features of
 //                            one token): data[p][src] holds src's bf16 partial of y
 // (max_rows, max_out) are fixed for a buffer's lifetime and passed with every call.
+//
+// Push / pull split (gdn_linear_push + gdn_pull_add_rmsnorm): the projection kernel only sends its
+// segments and raises their flags (no wait, so no limit on how many clusters are resident), and
+// the kernel that follows it in the decode step -- residual add and the next RMSNorm -- waits for
+// the flags, sums the ranks' partials in rank order, adds the residual and normalizes, in one pass
+// per token row.  The parity argument above holds with "call" = one push and its pull.
 // The data of a segment sits at an address fixed by (segment, token), whatever the call's shape,
 // and the epoch of segment g counts the calls that touched it, identically on every rank.  Parity
 // p = epoch & 1 double-buffers the data: a rank writes segment g of call e + 2 only after its own
@@ -71,6 +77,7 @@ struct Params {
   int64_t max_octs;       // 8-feature groups per rank's slot (max_out / 8)
   uint32_t spin_limit;
   int32_t* err;
+  int push_only;          // world > 1: send the partials and flags, leave the sum to add_rmsnorm_kernel
 };
 
 __device__ __forceinline__ uint32_t cluster_rank() {
@@ -313,7 +320,7 @@ __global__ void __launch_bounds__(kThreads) linear_kernel(const __grid_constant_
       if (gseg0 + sg < segs_total)
         st_release_sys(flag_at(p.bufs[dst], int(s_epoch[sg] & 1u), p.rank, gseg0 + sg), s_epoch[sg]);
     }
-    if (tid < nseg * p.world) {
+    if (!p.push_only && tid < nseg * p.world) {
       const int sg = tid / p.world, src = tid - sg * p.world;
       if (gseg0 + sg < segs_total) {
         const uint32_t e = s_epoch[sg];
@@ -330,7 +337,7 @@ __global__ void __launch_bounds__(kThreads) linear_kernel(const __grid_constant_
       }
     }
     __syncthreads();
-    if (s_ok) {
+    if (s_ok && !p.push_only) {
       for (int v = tid; v < nvec; v += kThreads) {
         const int o = v / n, j = v - o * n;
         const int f = feat0 + o * 8;
@@ -510,8 +517,9 @@ static int launch(const void* x, int64_t x_rs, const void* w, int64_t w_rs, void
   if (splits < 0 || splits > kMaxSplits) return fail(GDN_ERR_ARG, "%s: splits = %d (0 = auto, 1..8)", what, splits);
   int rc = set_smem_attr();
   if (rc) return rc;
-  const Plan pl = plan(n, n_out, k, splits, prm.world > 1);
-  if (prm.world > 1 && max_clusters(pl.splits, pl.smem) < pl.m_tiles)
+  const bool waits = prm.world > 1 && !prm.push_only;
+  const Plan pl = plan(n, n_out, k, splits, waits);
+  if (waits && max_clusters(pl.splits, pl.smem) < pl.m_tiles)
     return fail(GDN_ERR_SHAPE, "%s: %d tiles of %d CTAs do not fit the device at once", what, pl.m_tiles, pl.splits);
   CUtensorMap mw, mx;
   rc = make_map(&mw, w, n_out, k, w_rs, kBM, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
@@ -609,4 +617,220 @@ extern "C" int gdn_linear_allreduce(const void* x, int64_t x_rs, const void* w, 
     }
   }
   return lin::launch(x, x_rs, w, w_rs, y, y_rs, n, n_out, k, splits, prm, as_stream(stream), "gdn_linear_allreduce");
+}
+
+// ---------------------------------------------------------------------------------------------
+// Residual add fused with the next RMSNorm, and (PULL) with the sum over ranks of pushed partials.
+//
+//   h   = PULL ? bf16(sum over src, rank order, of fp32(data[src] row j))   (the all-reduce output)
+//              : h[j]                                                          (this rank's GEMM output)
+//   x[j] = bf16(x[j] + h)                                     (the residual stream, updated in place)
+//   out[j] = bf16((x[j] * rsqrt(mean(x[j]^2) + eps)) * (1 + w))
+//
+// One CTA of 128 threads per token row, with exactly the element-to-thread map, summation order
+// and arithmetic of rmsnorm_kernel, so the result is bit for bit that of the unfused sequence
+// all-reduce -> x + h -> Qwen3_5RMSNorm (src/cb_engine.py:295-355 runs them as separate ops).
+namespace gdn {
+namespace lin {
+
+struct AddNormParams {
+  __nv_bfloat16* x;
+  int64_t x_rs;
+  const __nv_bfloat16* h;
+  int64_t h_rs;
+  const __nv_bfloat16* w;
+  __nv_bfloat16* out;
+  int64_t out_rs;
+  int dim;
+  float eps;
+  int rank, world;
+  char* bufs[kMaxWorld];
+  int64_t max_rows, max_octs;
+  uint32_t spin_limit;
+  int32_t* err;
+};
+
+template <bool PULL>
+__global__ void __launch_bounds__(128) add_rmsnorm_kernel(const AddNormParams p) {
+  constexpr int NV = 8192 / (128 * 8);  // 8-element groups per thread at the largest dim
+  __shared__ float red[4];
+  __shared__ int s_ok;
+  const int tid = threadIdx.x, j = blockIdx.x;
+  const int octs = p.dim / 8;
+  char* own = PULL ? p.bufs[p.rank] : nullptr;
+  if (PULL) {
+    // every rank's partial of every segment of the row must be here: wait (bounded) for the flags
+    if (tid == 0) s_ok = 1;
+    __syncthreads();
+    const int nseg = (p.dim + kSegRows - 1) / kSegRows;
+    const volatile int32_t* verr = p.err;
+    for (int idx = tid; idx < nseg * p.world; idx += 128) {
+      const int g = idx / p.world, src = idx - g * p.world;
+      const uint32_t e = reinterpret_cast<const uint32_t*>(own)[g];
+      const uint32_t* f = flag_at(own, int(e & 1u), src, g);
+      uint32_t it = 0;
+      while (ld_acquire_sys(f) != e) {
+        if (++it > p.spin_limit || (verr && *verr != 0)) {
+          s_ok = 0;
+          break;
+        }
+        __nanosleep(64);
+      }
+      if (!s_ok) break;
+    }
+    __syncthreads();
+    if (!s_ok) {  // a rank did not arrive: report it and leave x and out alone
+      if (tid == 0 && p.err) atomicExch(p.err, 3);
+      return;
+    }
+  }
+  __nv_bfloat16* xr = p.x + int64_t(j) * p.x_rs;
+  float xv[NV][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int v = 0; v < NV; ++v) {
+    const int o = v * 128 + tid;
+    if (o < octs) {
+      float hv[8];
+      if (PULL) {
+        const uint32_t e = reinterpret_cast<const uint32_t*>(own)[o >> 1];
+        const int par = int(e & 1u);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) hv[i] = 0.f;
+        for (int src = 0; src < p.world; ++src) {
+          const uint4 u = reinterpret_cast<const uint4*>(own + kDataOff)[((int64_t(par) * p.world + src) * p.max_octs + o) *
+                                                                         p.max_rows + j];
+          add8(u, hv);
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) hv[i] = __bfloat162float(__float2bfloat16_rn(hv[i]));
+      } else {
+        const uint4 u = *reinterpret_cast<const uint4*>(p.h + int64_t(j) * p.h_rs + o * 8);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) hv[i] = 0.f;
+        add8(u, hv);
+      }
+      float xin[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) xin[i] = 0.f;
+      add8(*reinterpret_cast<const uint4*>(xr + o * 8), xin);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) xv[v][i] = __bfloat162float(__float2bfloat16_rn(xin[i] + hv[i]));
+      *reinterpret_cast<uint4*>(xr + o * 8) = pack8(xv[v]);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ss += xv[v][i] * xv[v][i];
+    }
+  }
+  ss = warp_sum(ss);
+  if ((tid & 31) == 0) red[tid >> 5] = ss;
+  __syncthreads();
+  const float r = 1.0f / sqrtf((red[0] + red[1] + red[2] + red[3]) / float(p.dim) + p.eps);
+  __nv_bfloat16* yr = p.out + int64_t(j) * p.out_rs;
+#pragma unroll
+  for (int v = 0; v < NV; ++v) {
+    const int o = v * 128 + tid;
+    if (o < octs) {
+      float wv[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) wv[i] = 0.f;
+      add8(*reinterpret_cast<const uint4*>(p.w + o * 8), wv);
+      float y[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) y[i] = (xv[v][i] * r) * (1.0f + wv[i]);
+      *reinterpret_cast<uint4*>(yr + o * 8) = pack8(y);
+    }
+  }
+}
+
+static int check_add_norm(const void* x, int64_t x_rs, const void* w, const void* out, int64_t out_rs, int64_t rows,
+                          int dim, int dtype, const char* what) {
+  if (dtype != GDN_BF16) return fail(GDN_ERR_DTYPE, "%s: dtype %d (bf16 only)", what, dtype);
+  if (rows < 1 || rows > 0x7fffffffLL || dim < 8 || dim > 8192 || dim % 8)
+    return fail(GDN_ERR_ARG, "%s: rows %lld, dim %d (a multiple of 8, <= 8192)", what, (long long)rows, dim);
+  if (!x || !w || !out) return fail(GDN_ERR_ARG, "%s: null pointer", what);
+  if (!aligned(x, 16) || !aligned(w, 16) || !aligned(out, 16) || x_rs % 8 || out_rs % 8 || x_rs < dim ||
+      out_rs < dim)
+    return fail(GDN_ERR_ARG, "%s: 16-byte aligned rows with strides that are multiples of 8 needed", what);
+  return GDN_OK;
+}
+
+}  // namespace lin
+}  // namespace gdn
+
+extern "C" int gdn_add_rmsnorm(void* x, int64_t x_rs, const void* h, int64_t h_rs, const void* weight, void* out,
+                               int64_t out_rs, int64_t rows, int dim, float eps, int dtype, void* stream) {
+  int rc = lin::check_add_norm(x, x_rs, weight, out, out_rs, rows, dim, dtype, "gdn_add_rmsnorm");
+  if (rc) return rc;
+  if (!h || !aligned(h, 16) || h_rs % 8 || h_rs < dim) return fail(GDN_ERR_ARG, "gdn_add_rmsnorm: h rows");
+  lin::AddNormParams p{};
+  p.x = static_cast<__nv_bfloat16*>(x);
+  p.x_rs = x_rs;
+  p.h = static_cast<const __nv_bfloat16*>(h);
+  p.h_rs = h_rs;
+  p.w = static_cast<const __nv_bfloat16*>(weight);
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.out_rs = out_rs;
+  p.dim = dim;
+  p.eps = eps;
+  p.world = 1;
+  lin::add_rmsnorm_kernel<false><<<unsigned(rows), 128, 0, as_stream(stream)>>>(p);
+  return check_launch("gdn_add_rmsnorm");
+}
+
+extern "C" int gdn_linear_push(const void* x, int64_t x_rs, const void* w, int64_t w_rs, int n, int n_out, int k,
+                               int splits, int rank, int world, void* const* bufs, int max_rows, int max_out,
+                               int32_t* err_flag, int dtype, void* stream) {
+  if (dtype != GDN_BF16) return fail(GDN_ERR_DTYPE, "gdn_linear_push: dtype %d (bf16 only)", dtype);
+  if (world < 2 || world > lin::kMaxWorld || rank < 0 || rank >= world)
+    return fail(GDN_ERR_ARG, "gdn_linear_push: rank %d of %d (world 2..%d)", rank, world, lin::kMaxWorld);
+  if (n > max_rows || n_out > max_out || max_out % 8 || max_out > lin::kMaxSegs * lin::kSegRows || max_rows < 1 ||
+      max_rows > lin::kMaxTokens)
+    return fail(GDN_ERR_ARG, "gdn_linear_push: %d x %d does not fit the buffers (max_rows %d, max_out %d)", n, n_out,
+                max_rows, max_out);
+  if (!bufs) return fail(GDN_ERR_ARG, "gdn_linear_push: null buffer table");
+  lin::Params prm{};
+  prm.rank = rank;
+  prm.world = world;
+  prm.max_rows = max_rows;
+  prm.max_octs = max_out / 8;
+  prm.err = err_flag;
+  prm.push_only = 1;
+  for (int r = 0; r < world; ++r) {
+    if (!bufs[r] || !aligned(bufs[r], 16)) return fail(GDN_ERR_ARG, "gdn_linear_push: buffer %d", r);
+    prm.bufs[r] = static_cast<char*>(bufs[r]);
+  }
+  // y is not written in push mode; x stands in as a valid, aligned pointer for the argument checks
+  return lin::launch(x, x_rs, w, w_rs, const_cast<void*>(x), n_out, n, n_out, k, splits, prm, as_stream(stream),
+                     "gdn_linear_push");
+}
+
+extern "C" int gdn_pull_add_rmsnorm(void* x, int64_t x_rs, const void* weight, void* out, int64_t out_rs, int64_t rows,
+                                    int dim, float eps, int rank, int world, void* const* bufs, int max_rows,
+                                    int max_out, uint32_t spin_limit, int32_t* err_flag, int dtype, void* stream) {
+  int rc = lin::check_add_norm(x, x_rs, weight, out, out_rs, rows, dim, dtype, "gdn_pull_add_rmsnorm");
+  if (rc) return rc;
+  if (world < 2 || world > lin::kMaxWorld || rank < 0 || rank >= world || !bufs)
+    return fail(GDN_ERR_ARG, "gdn_pull_add_rmsnorm: rank %d of %d (world 2..%d)", rank, world, lin::kMaxWorld);
+  if (rows > max_rows || dim > max_out || max_out % 8)
+    return fail(GDN_ERR_ARG, "gdn_pull_add_rmsnorm: %lld x %d does not fit the buffers", (long long)rows, dim);
+  lin::AddNormParams p{};
+  p.x = static_cast<__nv_bfloat16*>(x);
+  p.x_rs = x_rs;
+  p.w = static_cast<const __nv_bfloat16*>(weight);
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.out_rs = out_rs;
+  p.dim = dim;
+  p.eps = eps;
+  p.rank = rank;
+  p.world = world;
+  p.max_rows = max_rows;
+  p.max_octs = max_out / 8;
+  p.spin_limit = spin_limit ? spin_limit : (1u << 22);
+  p.err = err_flag;
+  for (int r = 0; r < world; ++r) {
+    if (!bufs[r] || !aligned(bufs[r], 16)) return fail(GDN_ERR_ARG, "gdn_pull_add_rmsnorm: buffer %d", r);
+    p.bufs[r] = static_cast<char*>(bufs[r]);
+  }
+  lin::add_rmsnorm_kernel<true><<<unsigned(rows), 128, 0, as_stream(stream)>>>(p);
+  return check_launch("gdn_pull_add_rmsnorm");
 }

@@ -126,6 +126,8 @@ class CBEngine:
         # tokens each step already copies to the host, so checking it costs no extra sync.
         self._err = torch.zeros(1, dtype=torch.int32, device=self.dev)
         self.graph_decode = graph_decode
+        if not hasattr(self, "peer_linear"):
+            self.peer_linear = None       # TPEngine sets its tensor-parallel exchange before this runs
         self._graphs, self._graph_out = {}, {}
         if graph_decode:
             self._capture_graphs()
@@ -185,7 +187,7 @@ class CBEngine:
         q, k = self.M.apply_rotary_pos_emb(q, k, cos, sin)
         o = ops.attn_decode(q[:, :, 0], k[:, :, 0], v[:, :, 0], self.kv_k[i], self.kv_v[i], self._slot, pos32, Lmax,
                             at.scaling, gate=gate, workspace=self._attn_ws, err=self._err)
-        return at.o_proj(o.reshape(n, 1, -1))
+        return o.reshape(n, 1, -1), at.o_proj
 
     def _gdn(self, gd, i, h):
         n = h.shape[0]
@@ -199,14 +201,29 @@ class CBEngine:
                                 self.rec[i], self._slot, p["norm_w"], p["eps"], p["Hk"], p["Hv"], p["dk"], p["dv"],
                                 ops.GDN_CONV_ELEM if ELEM_CONV else ops.GDN_CONV_HF, workspace=self._ws,
                                 err=self._err)
-        return gd.out_proj(core.reshape(n, 1, -1))
+        return core.reshape(n, 1, -1), gd.out_proj
 
-    def _mlp(self, i, mlp, h):
-        """The layer's MLP (down(act(gate(h)) * up(h))) with gate and up from one GEMM."""
+    def _mlp_act(self, i, mlp, h):
+        """The MLP up to its down projection, act(gate(h)) * up(h), with gate and up from one GEMM."""
         f = self._fused[i]
         I = f["inter"]
         y = F.linear(h, f["Wm"])
-        return mlp.down_proj(mlp.act_fn(y[..., :I]) * y[..., I:2 * I])
+        return mlp.act_fn(y[..., :I]) * y[..., I:2 * I]
+
+    def _proj_add_norm(self, proj, a, x, norm):
+        """A layer's output projection, the residual add and the next RMSNorm of the decode step:
+        x <- x + proj(a) in place; returns norm(x).  With a tensor-parallel exchange (``peer_linear``,
+        set by TPEngine) the projection pushes this rank's partial to every rank (gdn_linear_push)
+        and one kernel sums the ranks' partials, adds and normalizes (gdn_pull_add_rmsnorm);
+        otherwise the projection's own forward (cuBLAS, plus the all-reduce of AllReduceLinear under
+        TP) is followed by gdn_add_rmsnorm.  Both equal the reference's ``x = x + proj(a)`` and the
+        norm module of the next step (src/cb_engine.py:295-355)."""
+        ex = self.peer_linear
+        lin = getattr(proj, "lin", None)
+        if ex is not None and lin is not None and lin.bias is None and ex.applies(a, lin.weight):
+            ex.push(a, lin.weight)
+            return ex.pull_add_rmsnorm(x, norm.weight, norm.eps)
+        return ops.add_rmsnorm(x, proj(a), norm.weight, norm.eps)
 
     def _core(self, Lmax):
         """One decode step for all N slots from the static buffers (capturable)."""
@@ -215,17 +232,18 @@ class CBEngine:
         x = self.lm.embed_tokens(self._tok[:, None])
         pos3 = pos.view(1, N, 1).expand(3, N, 1)
         cos, sin = self.lm.rotary_emb(x, pos3)
-        for i, layer in enumerate(self.lm.layers):
-            h = layer.input_layernorm(x)
+        layers = self.lm.layers
+        h = layers[0].input_layernorm(x)
+        for i, layer in enumerate(layers):
             if self.cfg.layer_types[i] == "full_attention":
-                h = self._attn(layer.self_attn, i, h, cos, sin, pos32, Lmax)
+                a, proj = self._attn(layer.self_attn, i, h, cos, sin, pos32, Lmax)
             else:
-                h = self._gdn(layer.linear_attn, i, h)
-            x = x + h
-            x = x + self._mlp(i, layer.mlp, layer.post_attention_layernorm(x))
-        x = self.lm.norm(x)
+                a, proj = self._gdn(layer.linear_attn, i, h)
+            h = self._proj_add_norm(proj, a, x, layer.post_attention_layernorm)
+            nxt = layers[i + 1].input_layernorm if i + 1 < len(layers) else self.lm.norm
+            h = self._proj_add_norm(layer.mlp.down_proj, self._mlp_act(i, layer.mlp, h), x, nxt)
         # next tokens and, as the last entry, the error flag after this step's kernels
-        return torch.cat([self._greedy(x[:, 0]), self._err.to(torch.long)])
+        return torch.cat([self._greedy(h[:, 0]), self._err.to(torch.long)])
 
     def _greedy(self, h):
         """Greedy next token per row of the final hidden states (a vocabulary-parallel head

@@ -464,3 +464,22 @@ def linear_plan(n, n_out, k, splits=0, world=1):
     out = (ctypes.c_int32 * 5)()
     _lib.check(_lib.load().gdn_linear_plan(n, n_out, k, splits, world, out), "gdn_linear_plan")
     return dict(zip(("splits", "stages", "smem", "tiles", "kblocks"), list(out)))
+
+
+def add_rmsnorm(x: torch.Tensor, h: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+    """The residual add and the next layer norm of a decode step in one kernel (gdn_add_rmsnorm):
+    x <- bf16(x + h) IN PLACE, returns rmsnorm(x) = bf16(x * rsqrt(mean(x^2) + eps) * (1 + weight)),
+    bit for bit ``x = x + h; ops.rmsnorm(x, weight, eps)`` (src/cb_engine.py:295-355)."""
+    _need_cuda(x, h, weight)
+    dim = x.shape[-1]
+    x2, h2 = x.view(-1, dim), h.reshape(-1, dim)
+    if h2.stride(-1) != 1 or h2.stride(0) % 8 or h2.data_ptr() % 16:
+        h2 = h2.contiguous()
+    w = weight.to(x.dtype).contiguous()
+    y = torch.empty(x2.shape, dtype=x.dtype, device=x.device) if out is None else out.view(-1, dim)
+    _lib.check(_lib.load().gdn_add_rmsnorm(_p(x2), x2.stride(0), _p(h2), h2.stride(0), _p(w), _p(y), y.stride(0),
+                                           x2.shape[0], dim, float(eps), _dtype_code(x), _stream()),
+               "gdn_add_rmsnorm")
+    return y.view(x.shape)
+

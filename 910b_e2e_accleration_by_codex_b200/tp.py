@@ -142,6 +142,31 @@ class PeerLinearAllReduce(_PeerBuffers):
                    "gdn_linear_allreduce")
         return y.view(*x.shape[:-1], n_out)
 
+    def push(self, x, weight, splits=0):
+        """First half of ``self(x, weight)``: this rank's bf16 partial and its flags go to every rank
+        (gdn_linear_push).  Must be followed by ``pull_add_rmsnorm`` of the same shape."""
+        x2, w = ops._linear_operands(x, weight)
+        n, n_out, k = x2.shape[0], w.shape[0], x2.shape[1]
+        _lib.check(self.lib.gdn_linear_push(x2.data_ptr(), x2.stride(0), w.data_ptr(), w.stride(0), n, n_out, k,
+                                            int(splits), self.rank, self.world, self._table, self.max_rows,
+                                            self.max_out, self.err.data_ptr(), _lib.GDN_BF16,
+                                            torch.cuda.current_stream().cuda_stream), "gdn_linear_push")
+
+    def pull_add_rmsnorm(self, x, weight, eps, out=None):
+        """Second half: h = the sum over ranks of the pushed partials; x <- bf16(x + h) IN PLACE;
+        returns rmsnorm(x) (gdn_pull_add_rmsnorm).  x: [rows, dim] contiguous bf16, dim = the pushed
+        n_out."""
+        dim = x.shape[-1]
+        x2 = x.view(-1, dim)
+        w = weight.to(x.dtype).contiguous()
+        y = torch.empty(x2.shape, dtype=x.dtype, device=x.device) if out is None else out.view(-1, dim)
+        _lib.check(self.lib.gdn_pull_add_rmsnorm(x2.data_ptr(), x2.stride(0), w.data_ptr(), y.data_ptr(), y.stride(0),
+                                                 x2.shape[0], dim, float(eps), self.rank, self.world, self._table,
+                                                 self.max_rows, self.max_out, self.spin_limit, self.err.data_ptr(),
+                                                 _lib.GDN_BF16, torch.cuda.current_stream().cuda_stream),
+                   "gdn_pull_add_rmsnorm")
+        return y.view(x.shape)
+
 
 _PEER_AR = None
 

@@ -91,8 +91,10 @@ def parse():
                     help="after the model leg, profile graph-replayed decode steps (torch.profiler, device time "
                          "per kernel) and report a per-category breakdown")
     ap.add_argument("--model-gen", type=int, default=512, help="greedy tokens per turn of the model leg")
-    ap.add_argument("--model-allreduce", choices=["peer", "nccl"], default="peer",
-                    help="TP decode sums: this library's peer-memory kernel or NCCL")
+    ap.add_argument("--model-allreduce", choices=["fused", "peer", "nccl"], default="peer",
+                    help="TP decode sums: the row-parallel projection pushing its partial to every rank and the "
+                         "residual add + RMSNorm summing them (gdn_linear_push + gdn_pull_add_rmsnorm), cuBLAS + "
+                         "this library's peer-memory all-reduce, or cuBLAS + NCCL")
     return ap.parse_args()
 
 
@@ -634,6 +636,8 @@ def decode_breakdown(eng, slots, steps=8, ctx=500):
     cats = [("gdn decode layer (decode_prep + decode_state)", ("decode_prep_kernel", "decode_state_kernel")),
             ("attention decode (attn_decode + combine)", ("attn_decode_kernel", "attn_combine_kernel")),
             ("peer all-reduce (gdn_allreduce)", ("allreduce_bf16_kernel",)),
+            ("tcgen05 projection (gdn_linear / gdn_linear_push)", ("linear_kernel",)),
+            ("residual add + RMSNorm (gdn_add_rmsnorm / gdn_pull_add_rmsnorm)", ("add_rmsnorm_kernel",)),
             ("NCCL", ("nccl",)),
             ("layer RMSNorm (gdn_rmsnorm)", ("rmsnorm_kernel",)),
             ("GEMM (cuBLAS)", ("gemm", "nvjet", "xmma", "cublas", "cutlass", "gemv", "splitkreduce")),
@@ -694,8 +698,9 @@ def run_model(args, world, rank, local):
     reqs = serve.synthetic_requests(n_req, MODEL_TEXT_CONFIG["vocab_size"], seed=4321, max_turns=args.model_turns)
     bucket = eng_mod.GRAPH_BUCKET
     t_max = -(-(serve.max_context(reqs, args.model_gen) + 1) // bucket) * bucket
-    peer = args.model_allreduce == "peer"
-    eng = (tp_mod.TPEngine(model, slots, t_max, dev, world, graph_decode=True, peer_allreduce=peer) if world > 1
+    peer = args.model_allreduce in ("peer", "fused")
+    eng = (tp_mod.TPEngine(model, slots, t_max, dev, world, graph_decode=True, peer_allreduce=peer,
+                           fused_linear=args.model_allreduce == "fused") if world > 1
            else eng_mod.CBEngine(model, slots, t_max, dev, graph_decode=True))
     build_s = time.time() - t_build
     # warm-up: single-turn requests of the same prompt lengths through the same loop (GEMM shapes,
@@ -757,6 +762,8 @@ def run_model(args, world, rank, local):
            "timing": "wall clock per engine call (each ends with its host read of the tokens), max over ranks",
            "graph": True, "weights": "random-init bf16",
            "allreduce": ("none" if world <= 1 else
+                         "gdn_linear_push + gdn_pull_add_rmsnorm (peer memory) for decode, NCCL for prefill"
+                         if args.model_allreduce == "fused" else
                          "gdn_allreduce (peer memory) for decode, NCCL for prefill" if peer else "NCCL"),
            "lm_head": "vocabulary-parallel" if world > 1 else "full", "build_s": build_s}
     if parity is not None:

@@ -358,6 +358,31 @@ GDN_API int gdn_linear_allreduce(const void* x, int64_t x_rs, const void* w, int
                                  int max_rows, int max_out, uint32_t spin_limit, int32_t* err_flag, int dtype,
                                  void* stream);
 
+/* f1, split in two for the decode step.  gdn_linear_push is the projection of
+ * gdn_linear_allreduce without the wait and the sum: each rank's bf16
+ * partial and its flags go to every rank's exchange buffer (so the launch has
+ * no residency limit).  gdn_pull_add_rmsnorm then finishes the sum where the
+ * decode step continues -- the residual add and the next RMSNorm (the
+ * AllReduceLinear output, x + h and Qwen3_5RMSNorm of src/cb_engine.py:
+ * 295-355, src/cb_tp.py:25-35) -- in one kernel per token row: it waits
+ * (bounded) for every rank's flags of the row's segments, h = bf16(sum of the
+ * ranks' partials in rank order), x[j] = bf16(x[j] + h) in place and out[j] =
+ * bf16(x[j] * rsqrt(mean(x[j]^2) + eps) * (1 + w)), bit for bit the unfused
+ * all-reduce -> add -> gdn_rmsnorm.  Every push must be followed by its pull
+ * (same buffers, n_out = dim, rows = n) before the next push.  A rank that does
+ * not arrive makes the others set *err_flag = 3 and leave x and out alone.
+ * gdn_add_rmsnorm is the same residual add + RMSNorm with h given (one rank).
+ * bf16 only; dim a multiple of 8 and <= 8192; rows 16-byte aligned.
+ */
+GDN_API int gdn_linear_push(const void* x, int64_t x_rs, const void* w, int64_t w_rs, int n, int n_out, int k,
+                            int splits, int rank, int world, void* const* bufs, int max_rows, int max_out,
+                            int32_t* err_flag, int dtype, void* stream);
+GDN_API int gdn_pull_add_rmsnorm(void* x, int64_t x_rs, const void* weight, void* out, int64_t out_rs, int64_t rows,
+                                 int dim, float eps, int rank, int world, void* const* bufs, int max_rows,
+                                 int max_out, uint32_t spin_limit, int32_t* err_flag, int dtype, void* stream);
+GDN_API int gdn_add_rmsnorm(void* x, int64_t x_rs, const void* h, int64_t h_rs, const void* weight, void* out,
+                            int64_t out_rs, int64_t rows, int dim, float eps, int dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

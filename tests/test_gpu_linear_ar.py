@@ -9,9 +9,12 @@ bf16(sum over r of fp32(gdn_linear(x_r, W_r)))
 call to call (the per-segment epochs and the double-buffered slots must stay in step; outputs
 narrower than the buffers; 1-128 tokens), the calls are also captured in a CUDA graph and replayed
 with fresh inputs, and the result is compared with F.linear + NCCL all-reduce within bf16
-tolerance.  A second instance with a short spin limit checks the failure path: only rank 0 calls,
-its wait runs out, it reports error 3 and leaves y unwritten, while the other ranks wait in a host
-barrier (buffers mapped, no kernel in flight).  Skipped when fewer than two GPUs are visible.
+tolerance.  The push / pull split (gdn_linear_push, then gdn_pull_add_rmsnorm summing the ranks,
+adding the residual and normalizing) must equal the all-reduce output added to the residual in bf16
+and ops.rmsnorm BIT FOR BIT, eagerly, mixed with full fused calls, and captured in a graph.  A second
+instance with a short spin limit checks the failure path: only rank 0 calls, its waits run out (in
+the fused call, and in the pull after a push), it reports error 3 and leaves y / x / out unwritten,
+while the other ranks wait in a host barrier (buffers mapped, no kernel in flight).  Skipped when fewer than two GPUs are visible.
 """
 import os
 import socket
@@ -48,8 +51,10 @@ def _rank(rank, world, port, q):
     dev = torch.device("cuda", rank)
     out = {}
 
-    def expected(x, w):
-        S = ops.linear_plan(x.shape[0], w.shape[0], x.shape[1], world=world)["splits"]
+    def expected(x, w, waits=True):
+        # the split count of the launch: the fused call (which waits for the other ranks) keeps all
+        # its clusters resident; the push (no wait) plans as a one-rank projection
+        S = ops.linear_plan(x.shape[0], w.shape[0], x.shape[1], world=world if waits else 1)["splits"]
         part = ops.linear(x, w, splits=S)             # this rank's bf16 partial, same split count
         parts = [torch.empty_like(part) for _ in range(world)]
         dist.all_gather(parts, part)
@@ -105,6 +110,53 @@ def _rank(rank, world, port, q):
                 ok &= torch.equal(ys[i], expected(xs[i], ws[i]))
         out["graph"] = ok
         del graph
+        # push / pull split: the projection sends its partial, the residual add + RMSNorm sums the
+        # ranks (bit for bit: all-reduce output, x + h in bf16, then ops.rmsnorm)
+        nw = (torch.randn(HIDDEN, generator=torch.Generator().manual_seed(3)) * 0.1).to(torch.bfloat16).to(dev)
+        ok = True
+        for rep in range(2):
+            for case, (n, n_out, k) in enumerate([CASES[0], CASES[4], CASES[1], CASES[3]]):
+                x, w = (t.to(dev) for t in inp(rank, 300 + 10 * rep + case, n, n_out, k))
+                res = (torch.randn(n, HIDDEN, generator=torch.Generator().manual_seed(77 + case)) * 2).to(
+                    torch.bfloat16).to(dev)
+                ref_x = res + expected(x, w, waits=False)
+                ref_out = ops.rmsnorm(ref_x, nw, 1e-6)
+                fl.push(x, w)
+                got = fl.pull_add_rmsnorm(res, nw, 1e-6)
+                ok &= torch.equal(res, ref_x) and torch.equal(got, ref_out)
+                if case == 1:                # a full fused call between push/pull pairs
+                    ok &= torch.equal(fl(x, w), expected(x, w))
+        out["push_pull"] = bool(ok)
+        # push / pull captured in a graph (two pairs), replayed with fresh inputs
+        pshapes = [CASES[0], CASES[1]]
+        pxs = [torch.zeros(n, k, dtype=torch.bfloat16, device=dev) for n, _, k in pshapes]
+        pws = [torch.zeros(n_out, k, dtype=torch.bfloat16, device=dev) for _, n_out, k in pshapes]
+        pres = torch.zeros(32, HIDDEN, dtype=torch.bfloat16, device=dev)
+        s.wait_stream(torch.cuda.current_stream())
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(graph, stream=s):
+                fl.push(pxs[0], pws[0])
+                pout1 = fl.pull_add_rmsnorm(pres, nw, 1e-6)
+                fl.push(pxs[1], pws[1])
+                pout2 = fl.pull_add_rmsnorm(pres, nw, 1e-6)
+        torch.cuda.current_stream().wait_stream(s)
+        ok = True
+        for rep in range(3):
+            for i, (n, n_out, k) in enumerate(pshapes):
+                x, w = inp(rank, 700 + 10 * rep + i, n, n_out, k)
+                pxs[i].copy_(x)
+                pws[i].copy_(w)
+            r0 = (torch.randn(32, HIDDEN, generator=torch.Generator().manual_seed(800 + rep))).to(torch.bfloat16)
+            pres.copy_(r0)
+            graph.replay()
+            torch.cuda.synchronize()
+            x1 = r0.to(dev) + expected(pxs[0], pws[0], waits=False)
+            x2 = x1 + expected(pxs[1], pws[1], waits=False)
+            o2 = ops.rmsnorm(x2, nw, 1e-6)
+            ok &= torch.equal(pres, x2) and torch.equal(pout2, o2) and torch.equal(pout1, ops.rmsnorm(x1, nw, 1e-6))
+        out["push_pull_graph"] = bool(ok)
+        del graph
         out["err"] = int(fl.err.item())
         out["applies_big"] = fl.applies(torch.zeros(MAX_ROWS + 1, 64, dtype=torch.bfloat16, device=dev),
                                         torch.zeros(64, 64, dtype=torch.bfloat16, device=dev))
@@ -116,6 +168,12 @@ def _rank(rank, world, port, q):
             y = fl2(x, w)
             torch.cuda.synchronize()
             out["timeout_err"] = int(fl2.err.item())
+            fl2.err.zero_()
+            res = torch.ones(16, 1024, dtype=torch.bfloat16, device=dev)
+            fl2.push(x, w)
+            o = fl2.pull_add_rmsnorm(res, torch.ones(1024, dtype=torch.bfloat16, device=dev), 1e-6)
+            torch.cuda.synchronize()
+            out["pull_timeout"] = int(fl2.err.item()) == 3 and bool((res == 1).all())
         dist.barrier()                       # the other ranks wait here while rank 0's kernel runs
         fl2.close()
         q.put((rank, out))
@@ -149,5 +207,6 @@ def test_fused_linear_allreduce_multi_gpu():
     res = dict(q.get(timeout=5) for _ in range(world))
     for r in range(world):
         assert res[r]["eager"] and res[r]["same"] and res[r]["graph"] and res[r]["nccl_close"], res[r]
+        assert res[r]["push_pull"] and res[r]["push_pull_graph"], res[r]
         assert res[r]["err"] == 0 and not res[r]["applies_big"], res[r]
-    assert res[0]["timeout_err"] == 3, res[0]
+    assert res[0]["timeout_err"] == 3 and res[0]["pull_timeout"], res[0]
