@@ -47,6 +47,8 @@ SIGNATURES = {
                                        _vp, _vp, _vp, _vp, _vp, _i64, _vp, _i64, _i32, _i32, _i32, _i32, _i32,
                                        _i32, _vp, _vp]),
     "gdn_rmsnorm": (_i32, [_vp, _i64, _vp, _vp, _i64, _i64, _i32, _f32, _i32, _vp]),
+    "gdn_attn_decode_prep": (_i32, [_vp, _i64, _vp, _vp, _f32, _vp, _vp, _i64, _i32, _vp, _vp, _vp, _vp, _i32,
+                                    _i32, _i32, _i32, _i32, _vp]),
     "gdn_attn_decode_workspace_size": (_sz, [_i32, _i32, _i32, _i32]),
     "gdn_attn_decode": (_i32, [_vp, _vp, _vp, _vp, _vp, _i64, _i32, _vp, _vp, _i32, _vp, _f32, _vp, _i32, _i32,
                                _i32, _i32, _vp, _sz, _i32, _vp, _vp]),
@@ -67,6 +69,7 @@ SIGNATURES = {
     "gdn_pull_add_rmsnorm": (_i32, [_vp, _i64, _vp, _vp, _i64, _i64, _i32, _f32, _i32, _i32, _vp, _i32, _i32,
                                     C.c_uint32, _vp, _i32, _vp]),
     "gdn_add_rmsnorm": (_i32, [_vp, _i64, _vp, _i64, _vp, _vp, _i64, _i64, _i32, _f32, _i32, _vp]),
+    "gdn_silu_mul": (_i32, [_vp, _i64, _i32, _vp, _i64, _i64, _i32, _vp]),
 }
 GDN_IPC_HANDLE_BYTES = 64
 

@@ -289,3 +289,165 @@ extern "C" int gdn_attn_decode(const void* q, const void* k_new, const void* v_n
   attn::attn_combine_kernel<<<unsigned(int64_t(n) * Hq), attn::kMaxHd, 0, s>>>(p);
   return check_launch("gdn_attn_decode (combine)");
 }
+
+// ---------------------------------------------------------------------------------------------
+// The attention layer's decode preamble in one kernel (CBEngine._attn before the attention itself,
+// src/cb_engine.py:295-316, with HF's Qwen3_5Attention pieces): from one token row of the fused
+// q|gate, k, v projection it writes the four contiguous inputs of gdn_attn_decode:
+//   q    = rotary(q_norm(q_h))   per query head   (q_h = y[2 hd h : 2 hd h + hd])
+//   gate = y[2 hd h + hd : 2 hd (h + 1)]          (the chunk of the q|gate view)
+//   k    = rotary(k_norm(k_h))   per kv head      (k_h = y[nq + hd h : ...])
+//   v    = y[nq + nk + hd h : ...]
+// q_norm / k_norm are Qwen3_5RMSNorm over head_dim with the element order, reduction order and
+// rounding of gdn_rmsnorm (one warp per head; lane t holds elements 8t .. 8t + 7), and rotary is
+// apply_rotary_pos_emb on the first rd dims with every bf16 rounding of the torch ops:
+//   out[i] = bf16(bf16(x[i] cos[i]) + bf16(rot[i] sin[i])),  rot = cat(-x[rd/2:rd], x[:rd/2]),
+// dims rd.. passed through.  So the result equals the sequence of torch ops bit for bit.
+// One warp per (token, head) over Hq + kvh heads; another warp per head copies v and gate.
+namespace gdn {
+namespace attn {
+
+struct PrepParams {
+  const __nv_bfloat16* y;
+  int64_t y_rs;
+  const __nv_bfloat16* qw;
+  const __nv_bfloat16* kw;
+  const __nv_bfloat16* cos;
+  const __nv_bfloat16* sin;
+  int64_t cs_rs;
+  __nv_bfloat16 *q, *k, *v, *gate;
+  int n, Hq, kvh, hd, rd;
+  float eps;
+};
+
+__device__ __forceinline__ void unpack8f(const uint4& u, float* x) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    x[2 * i] = __uint_as_float(w[i] << 16);
+    x[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+  }
+}
+__device__ __forceinline__ float r16(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+__device__ __forceinline__ uint4 pack8f(const float* a) {
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    __nv_bfloat162 t = __floats2bfloat162_rn(a[2 * i], a[2 * i + 1]);
+    w[i] = *reinterpret_cast<uint32_t*>(&t);
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+__global__ void __launch_bounds__(128) attn_prep_kernel(const PrepParams p) {
+  const int lane = threadIdx.x & 31;
+  const int64_t task = int64_t(blockIdx.x) * 4 + (threadIdx.x >> 5);
+  const int heads = p.Hq + p.kvh;
+  const int64_t norm_tasks = int64_t(p.n) * heads;
+  const int groups = p.hd / 8;  // 8-element groups per head (<= 32)
+  if (task < norm_tasks) {
+    const int j = int(task / heads), h = int(task - int64_t(j) * heads);
+    const bool isq = h < p.Hq;
+    const int hh = isq ? h : h - p.Hq;
+    const __nv_bfloat16* src = p.y + int64_t(j) * p.y_rs +
+                               (isq ? int64_t(2) * p.hd * hh : int64_t(2) * p.hd * p.Hq + int64_t(p.hd) * hh);
+    const __nv_bfloat16* w = isq ? p.qw : p.kw;
+    float x[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f}, wv[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    float ss = 0.f;
+    if (lane < groups) {
+      unpack8f(*reinterpret_cast<const uint4*>(src + lane * 8), x);
+      unpack8f(*reinterpret_cast<const uint4*>(w + lane * 8), wv);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ss += x[i] * x[i];
+    }
+    ss = warp_sum(ss);
+    const float r = 1.0f / sqrtf(ss / float(p.hd) + p.eps);
+    float xn[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) xn[i] = r16((x[i] * r) * (1.0f + wv[i]));
+    // rotary on dims [0, rd): the rotate_half partner of element i sits rd/16 lanes away
+    const int half = p.rd / 16;
+    float other[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int src_lane = lane < half ? lane + half : lane - half;
+      other[i] = __shfl_sync(0xffffffffu, xn[i], src_lane < 32 ? src_lane : lane);
+    }
+    float out[8];
+    if (lane * 8 < p.rd) {
+      const __nv_bfloat16* cs = p.cos + int64_t(j) * p.cs_rs + lane * 8;
+      const __nv_bfloat16* sn = p.sin + int64_t(j) * p.cs_rs + lane * 8;
+      float c[8], s[8];
+      unpack8f(*reinterpret_cast<const uint4*>(cs), c);
+      unpack8f(*reinterpret_cast<const uint4*>(sn), s);
+      const bool first = lane < half;  // rot = -x[i + rd/2] for i < rd/2, x[i - rd/2] above
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float rot = first ? -other[i] : other[i];
+        out[i] = r16(r16(xn[i] * c[i]) + r16(rot * s[i]));
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) out[i] = xn[i];
+    }
+    if (lane < groups) {
+      __nv_bfloat16* dst = (isq ? p.q + (int64_t(j) * p.Hq + hh) * p.hd : p.k + (int64_t(j) * p.kvh + hh) * p.hd);
+      *reinterpret_cast<uint4*>(dst + lane * 8) = pack8f(out);
+    }
+    return;
+  }
+  // copies: v heads and gate heads
+  const int64_t c = task - norm_tasks;
+  if (c >= norm_tasks || lane >= groups) return;
+  const int j = int(c / heads), h = int(c - int64_t(j) * heads);
+  const __nv_bfloat16* row = p.y + int64_t(j) * p.y_rs;
+  if (h < p.Hq) {
+    const uint4 u = *reinterpret_cast<const uint4*>(row + int64_t(2) * p.hd * h + p.hd + lane * 8);
+    *reinterpret_cast<uint4*>(p.gate + (int64_t(j) * p.Hq + h) * p.hd + lane * 8) = u;
+  } else {
+    const int hh = h - p.Hq;
+    const uint4 u = *reinterpret_cast<const uint4*>(row + int64_t(2) * p.hd * p.Hq + int64_t(p.hd) * p.kvh +
+                                                    int64_t(p.hd) * hh + lane * 8);
+    *reinterpret_cast<uint4*>(p.v + (int64_t(j) * p.kvh + hh) * p.hd + lane * 8) = u;
+  }
+}
+
+}  // namespace attn
+}  // namespace gdn
+
+extern "C" int gdn_attn_decode_prep(const void* y, int64_t y_rs, const void* q_norm_w, const void* k_norm_w, float eps,
+                                    const void* cos, const void* sin, int64_t cs_rs, int rd, void* q, void* k, void* v,
+                                    void* gate, int n, int Hq, int kvh, int hd, int dtype, void* stream) {
+  using namespace gdn;
+  if (dtype != GDN_BF16) return fail(GDN_ERR_DTYPE, "gdn_attn_decode_prep: dtype %d (bf16 only)", dtype);
+  if (n < 0 || Hq < 1 || kvh < 1 || hd < 8 || hd > 256 || hd % 8 || rd < 0 || rd > hd || rd % 16 || (rd == 0))
+    return fail(GDN_ERR_ARG, "gdn_attn_decode_prep: Hq %d kvh %d hd %d rd %d (hd a multiple of 8 <= 256; rd a "
+                             "multiple of 16 in 16..hd)", Hq, kvh, hd, rd);
+  if (n == 0) return GDN_OK;
+  const void* ptrs[] = {y, q_norm_w, k_norm_w, cos, sin, q, k, v, gate};
+  for (const void* ptr : ptrs)
+    if (!ptr || !aligned(ptr, 16)) return fail(GDN_ERR_ARG, "gdn_attn_decode_prep: null or misaligned pointer");
+  if (y_rs % 8 || cs_rs % 8 || y_rs < int64_t(2) * Hq * hd + int64_t(2) * kvh * hd || cs_rs < rd)
+    return fail(GDN_ERR_ARG, "gdn_attn_decode_prep: row strides");
+  attn::PrepParams p{};
+  p.y = static_cast<const __nv_bfloat16*>(y);
+  p.y_rs = y_rs;
+  p.qw = static_cast<const __nv_bfloat16*>(q_norm_w);
+  p.kw = static_cast<const __nv_bfloat16*>(k_norm_w);
+  p.cos = static_cast<const __nv_bfloat16*>(cos);
+  p.sin = static_cast<const __nv_bfloat16*>(sin);
+  p.cs_rs = cs_rs;
+  p.q = static_cast<__nv_bfloat16*>(q);
+  p.k = static_cast<__nv_bfloat16*>(k);
+  p.v = static_cast<__nv_bfloat16*>(v);
+  p.gate = static_cast<__nv_bfloat16*>(gate);
+  p.n = n;
+  p.Hq = Hq;
+  p.kvh = kvh;
+  p.hd = hd;
+  p.rd = rd;
+  p.eps = eps;
+  const int64_t tasks = 2 * int64_t(n) * (Hq + kvh);  // norm + rotary tasks, then copy tasks
+  attn::attn_prep_kernel<<<unsigned((tasks + 3) / 4), 128, 0, as_stream(stream)>>>(p);
+  return check_launch("gdn_attn_decode_prep");
+}

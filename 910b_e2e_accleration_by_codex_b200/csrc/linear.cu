@@ -685,37 +685,44 @@ __global__ void __launch_bounds__(128) add_rmsnorm_kernel(const AddNormParams p)
     }
   }
   __nv_bfloat16* xr = p.x + int64_t(j) * p.x_rs;
+  // every load of the row first (x, h or the ranks' partials, and the norm weight), then the
+  // stores: the in-place store of x must not hold back the loads behind it
+  uint4 xu[NV], wu[NV];
   float xv[NV][8];
+#pragma unroll
+  for (int v = 0; v < NV; ++v) {
+    const int o = v * 128 + tid;
+    if (o < octs) {
+      xu[v] = *reinterpret_cast<const uint4*>(xr + o * 8);
+      wu[v] = *reinterpret_cast<const uint4*>(p.w + o * 8);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) xv[v][i] = 0.f;
+      if (PULL) {
+        const uint32_t e = reinterpret_cast<const uint32_t*>(own)[o >> 1];
+        const int par = int(e & 1u);
+        for (int src = 0; src < p.world; ++src) {
+          const uint4 u = reinterpret_cast<const uint4*>(own + kDataOff)[((int64_t(par) * p.world + src) * p.max_octs + o) *
+                                                                         p.max_rows + j];
+          add8(u, xv[v]);
+        }
+      } else {
+        add8(*reinterpret_cast<const uint4*>(p.h + int64_t(j) * p.h_rs + o * 8), xv[v]);
+      }
+    }
+  }
   float ss = 0.f;
 #pragma unroll
   for (int v = 0; v < NV; ++v) {
     const int o = v * 128 + tid;
     if (o < octs) {
-      float hv[8];
-      if (PULL) {
-        const uint32_t e = reinterpret_cast<const uint32_t*>(own)[o >> 1];
-        const int par = int(e & 1u);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) hv[i] = 0.f;
-        for (int src = 0; src < p.world; ++src) {
-          const uint4 u = reinterpret_cast<const uint4*>(own + kDataOff)[((int64_t(par) * p.world + src) * p.max_octs + o) *
-                                                                         p.max_rows + j];
-          add8(u, hv);
-        }
-#pragma unroll
-        for (int i = 0; i < 8; ++i) hv[i] = __bfloat162float(__float2bfloat16_rn(hv[i]));
-      } else {
-        const uint4 u = *reinterpret_cast<const uint4*>(p.h + int64_t(j) * p.h_rs + o * 8);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) hv[i] = 0.f;
-        add8(u, hv);
-      }
       float xin[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) xin[i] = 0.f;
-      add8(*reinterpret_cast<const uint4*>(xr + o * 8), xin);
+      add8(xu[v], xin);
+      // h rounded to bf16 (the all-reduce output, or the GEMM output as given), then x + h rounded
 #pragma unroll
-      for (int i = 0; i < 8; ++i) xv[v][i] = __bfloat162float(__float2bfloat16_rn(xin[i] + hv[i]));
+      for (int i = 0; i < 8; ++i)
+        xv[v][i] = __bfloat162float(__float2bfloat16_rn(xin[i] + __bfloat162float(__float2bfloat16_rn(xv[v][i]))));
       *reinterpret_cast<uint4*>(xr + o * 8) = pack8(xv[v]);
 #pragma unroll
       for (int i = 0; i < 8; ++i) ss += xv[v][i] * xv[v][i];
@@ -733,7 +740,7 @@ __global__ void __launch_bounds__(128) add_rmsnorm_kernel(const AddNormParams p)
       float wv[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) wv[i] = 0.f;
-      add8(*reinterpret_cast<const uint4*>(p.w + o * 8), wv);
+      add8(wu[v], wv);
       float y[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) y[i] = (xv[v][i] * r) * (1.0f + wv[i]);

@@ -179,6 +179,15 @@ class CBEngine:
         f = self._fused[i]
         nq, nk, _ = f["sizes"]
         y = F.linear(h, f["W"])                       # [q | k | v] of one GEMM
+        rd = cos.shape[-1]
+        if (hd % 8 == 0 and hd <= 256 and rd % 16 == 0 and 16 <= rd <= hd and at.q_norm.eps == at.k_norm.eps
+                and y.dtype == torch.bfloat16):
+            # q/k norms, rotary and the layout attn_decode takes, in one kernel (bit for bit the ops below)
+            q, k, v, gate = ops.attn_decode_prep(y.view(n, -1), at.q_norm.weight, at.k_norm.weight, at.q_norm.eps,
+                                                 cos, sin, nq // (2 * hd), kvh, hd)
+            o = ops.attn_decode(q, k, v, self.kv_k[i], self.kv_v[i], self._slot, pos32, Lmax, at.scaling, gate=gate,
+                                workspace=self._attn_ws, err=self._err)
+            return o.reshape(n, 1, -1), at.o_proj
         qg = y[..., :nq].view(n, 1, -1, hd * 2)
         q, gate = torch.chunk(qg, 2, dim=-1)
         q = at.q_norm(q).transpose(1, 2)
@@ -208,6 +217,8 @@ class CBEngine:
         f = self._fused[i]
         I = f["inter"]
         y = F.linear(h, f["Wm"])
+        if type(mlp.act_fn).__name__ in ("SiLU", "SiLUActivation"):   # both are F.silu
+            return ops.silu_mul(y, I)         # one kernel for silu then product (bit for bit the same)
         return mlp.act_fn(y[..., :I]) * y[..., I:2 * I]
 
     def _proj_add_norm(self, proj, a, x, norm):

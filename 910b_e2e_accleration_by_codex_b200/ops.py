@@ -110,6 +110,29 @@ def attn_decode_workspace(n, Hq, hd, max_len, device):
     return torch.empty(max(nb, 16), dtype=torch.uint8, device=device)
 
 
+def attn_decode_prep(y, q_norm_w, k_norm_w, eps, cos, sin, Hq, kvh, hd):
+    """The attention decode preamble (gdn_attn_decode_prep): from the fused q|gate, k, v projection
+    y [n, >= 2 Hq hd + 2 kvh hd] returns (q, k, v, gate) = (rotary(q_norm(q)), rotary(k_norm(k)), v,
+    gate) as contiguous [n, heads, hd] tensors, bit for bit HF's q_norm / k_norm and
+    apply_rotary_pos_emb (cos / sin [n, ..., rd]) in bf16 (src/cb_engine.py:295-316)."""
+    _need_cuda(y, q_norm_w, k_norm_w, cos, sin)
+    n = y.shape[0]
+    y2 = y.reshape(n, -1)
+    if y2.stride(-1) != 1 or y2.stride(0) % 8 or y2.data_ptr() % 16:
+        y2 = y2.contiguous()
+    rd = cos.shape[-1]
+    c2, s2 = cos.reshape(n, rd).contiguous(), sin.reshape(n, rd).contiguous()
+    q = torch.empty(n, Hq, hd, dtype=y.dtype, device=y.device)
+    g = torch.empty(n, Hq, hd, dtype=y.dtype, device=y.device)
+    k = torch.empty(n, kvh, hd, dtype=y.dtype, device=y.device)
+    v = torch.empty(n, kvh, hd, dtype=y.dtype, device=y.device)
+    _lib.check(_lib.load().gdn_attn_decode_prep(_p(y2), y2.stride(0), _p(q_norm_w.contiguous()),
+                                                _p(k_norm_w.contiguous()), float(eps), _p(c2), _p(s2), c2.stride(0),
+                                                int(rd), _p(q), _p(k), _p(v), _p(g), n, Hq, kvh, hd, _dtype_code(y),
+                                                _stream()), "gdn_attn_decode_prep")
+    return q, k, v, g
+
+
 def attn_decode(q, k_new, v_new, kv_k, kv_v, slot_idx, pos, max_len, scale, gate=None, out=None, workspace=None,
                 err=None):
     """Slot-indexed attention decode over the KV pool (CBEngine._attn, src/cb_engine.py:295-316): writes
@@ -482,4 +505,17 @@ def add_rmsnorm(x: torch.Tensor, h: torch.Tensor, weight: torch.Tensor, eps: flo
                                            x2.shape[0], dim, float(eps), _dtype_code(x), _stream()),
                "gdn_add_rmsnorm")
     return y.view(x.shape)
+
+
+def silu_mul(y: torch.Tensor, inter: int, out: torch.Tensor | None = None) -> torch.Tensor:
+    """act_fn(gate) * up of Qwen3_5MLP on the fused gate|up projection y [..., 2*inter] (gdn_silu_mul):
+    bf16(bf16(silu(y[..., :inter])) * y[..., inter:2*inter]), bit for bit the two bf16 torch ops."""
+    _need_cuda(y)
+    y2 = y.reshape(-1, y.shape[-1])
+    if y2.stride(-1) != 1 or y2.stride(0) % 8 or y2.data_ptr() % 16:
+        y2 = y2.contiguous()
+    o = torch.empty(y2.shape[0], inter, dtype=y.dtype, device=y.device) if out is None else out.view(-1, inter)
+    _lib.check(_lib.load().gdn_silu_mul(_p(y2), y2.stride(0), int(inter), _p(o), o.stride(0), y2.shape[0],
+                                        _dtype_code(y), _stream()), "gdn_silu_mul")
+    return o.view(*y.shape[:-1], inter)
 

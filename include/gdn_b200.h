@@ -274,6 +274,21 @@ GDN_API int gdn_rmsnorm(const void* x, int64_t x_rs, const void* weight, void* y
  * gdn_attn_decode_workspace_size(n, Hq, hd, max_len) bytes.  A bad slot or
  * position sets *err_flag = 1 and yields zeros for that entry.
  */
+/* The attention layer's decode preamble in one call (CBEngine._attn before the
+ * attention, src/cb_engine.py:295-316): from the fused q|gate, k, v projection
+ * y [n, 2 Hq hd + 2 kvh hd] (per query head its hd query dims then its hd gate
+ * dims; then the kv heads of k, then of v) it writes gdn_attn_decode's inputs
+ * q [n, Hq, hd] = rotary(q_norm(q)), k [n, kvh, hd] = rotary(k_norm(k)),
+ * v [n, kvh, hd], gate [n, Hq, hd].  q_norm / k_norm: Qwen3_5RMSNorm over hd
+ * with gdn_rmsnorm's arithmetic; rotary: apply_rotary_pos_emb on the first rd
+ * dims with cos / sin [n, rd] (row stride cs_rs), each bf16 rounding of the
+ * torch ops kept -- bit for bit the torch sequence.  bf16; hd a multiple of 8
+ * and <= 256; rd a multiple of 16 in 16..hd; 16-byte aligned pointers.
+ */
+GDN_API int gdn_attn_decode_prep(const void* y, int64_t y_rs, const void* q_norm_w, const void* k_norm_w, float eps,
+                                 const void* cos, const void* sin, int64_t cs_rs, int rd, void* q, void* k, void* v,
+                                 void* gate, int n, int Hq, int kvh, int hd, int dtype, void* stream);
+
 GDN_API size_t gdn_attn_decode_workspace_size(int n, int Hq, int hd, int max_len);
 GDN_API int gdn_attn_decode(const void* q, const void* k_new, const void* v_new, void* kv_k, void* kv_v,
                             int64_t n_slots, int T, const int32_t* slot_idx, const int32_t* pos, int max_len,
@@ -382,6 +397,16 @@ GDN_API int gdn_pull_add_rmsnorm(void* x, int64_t x_rs, const void* weight, void
                                  int max_out, uint32_t spin_limit, int32_t* err_flag, int dtype, void* stream);
 GDN_API int gdn_add_rmsnorm(void* x, int64_t x_rs, const void* h, int64_t h_rs, const void* weight, void* out,
                             int64_t out_rs, int64_t rows, int dim, float eps, int dtype, void* stream);
+
+/* The MLP activation of the decode step, act_fn(gate) * up of Qwen3_5MLP
+ * (transformers modeling_qwen3_5.py; the reference runs HF's module,
+ * src/cb_engine.py:295-355), on the fused gate|up projection y [rows, 2*inter]
+ * (gate = y[:, :inter], up = y[:, inter:]): out = bf16(bf16(silu(gate)) * up),
+ * bit for bit the two bf16 torch ops.  bf16; inter a multiple of 8; 16-byte
+ * aligned rows.
+ */
+GDN_API int gdn_silu_mul(const void* y, int64_t y_rs, int inter, void* out, int64_t out_rs, int64_t rows, int dtype,
+                         void* stream);
 
 #ifdef __cplusplus
 }

@@ -1,4 +1,5 @@
-"""Residual add fused with the next layer norm (gdn_add_rmsnorm, ops.add_rmsnorm).
+"""Residual add fused with the next layer norm (gdn_add_rmsnorm, ops.add_rmsnorm), and the MLP
+activation silu(gate) * up in one kernel (gdn_silu_mul).
 
 The decode step's ``x = x + h`` followed by Qwen3_5RMSNorm runs as one kernel that keeps the
 element-to-thread map, summation order and arithmetic of the plain RMSNorm kernel, so it must equal
@@ -48,3 +49,40 @@ def test_add_rmsnorm_strided_rows():
     torch.cuda.synchronize()
     assert torch.equal(x, ref_x) and torch.equal(outb[:, 64:5184], ref)
     assert (outb[:, :64] == 0).all() and (outb[:, 5184:] == 0).all()
+
+
+@pytest.mark.parametrize("rows,inter", [(16, 17408), (128, 2176), (1, 8), (33, 4352)])
+def test_silu_mul_bit_exact(rows, inter):
+    ops = pkg("ops")
+    g = torch.Generator(device="cpu").manual_seed(rows + inter)
+    y = (torch.randn(rows, 1, 2 * inter + 8, generator=g) * 4).to(torch.bfloat16).to(DEV)   # padded fused rows
+    ref = torch.nn.functional.silu(y[..., :inter]) * y[..., inter:2 * inter]
+    got = ops.silu_mul(y, inter)
+    torch.cuda.synchronize()
+    assert torch.equal(got, ref)
+
+
+@pytest.mark.parametrize("n,Hq,kvh,hd,rd", [(16, 24, 4, 256, 64), (32, 12, 2, 256, 64), (128, 3, 1, 256, 64),
+                                           (5, 4, 1, 64, 16), (7, 2, 2, 128, 128)])
+def test_attn_decode_prep_bit_exact(n, Hq, kvh, hd, rd):
+    """q/k RMSNorm + partial rotary + the attn_decode layout in one kernel, against the torch
+    sequence of CBEngine._attn (the patched Qwen3_5RMSNorm and HF's apply_rotary_pos_emb)."""
+    from transformers.models.qwen3_5 import modeling_qwen3_5 as M
+    ops = pkg("ops")
+    g = torch.Generator(device="cpu").manual_seed(n * 7 + Hq + hd)
+    nq, nk = 2 * Hq * hd, kvh * hd
+    y = (torch.randn(n, 1, nq + 2 * nk + 8, generator=g) * 2).to(torch.bfloat16).to(DEV)   # padded fused rows
+    qw = (torch.randn(hd, generator=g) * 0.2).to(torch.bfloat16).to(DEV)
+    kw = (torch.randn(hd, generator=g) * 0.2).to(torch.bfloat16).to(DEV)
+    ang = torch.rand(n, 1, rd, generator=g) * 6.3
+    cos, sin = ang.cos().to(torch.bfloat16).to(DEV), ang.sin().to(torch.bfloat16).to(DEV)
+    qg = y[..., :nq].view(n, 1, -1, hd * 2)
+    q, gate = torch.chunk(qg, 2, dim=-1)
+    q = ops.rmsnorm(q, qw, 1e-6).transpose(1, 2)
+    k = ops.rmsnorm(y[..., nq:nq + nk].view(n, 1, kvh, hd), kw, 1e-6).transpose(1, 2)
+    v = y[..., nq + nk:nq + 2 * nk].view(n, 1, kvh, hd).transpose(1, 2)
+    q, k = M.apply_rotary_pos_emb(q, k, cos, sin)
+    gq, gk, gv, gg = ops.attn_decode_prep(y.view(n, -1), qw, kw, 1e-6, cos, sin, Hq, kvh, hd)
+    torch.cuda.synchronize()
+    assert torch.equal(gq, q[:, :, 0]) and torch.equal(gk, k[:, :, 0])
+    assert torch.equal(gv, v[:, :, 0]) and torch.equal(gg, gate.reshape(n, Hq, hd))
