@@ -81,6 +81,10 @@ def parse():
                     help="GDN layers in the decode leg's step (48 in config 2; fewer for short profiler captures)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="target CPU-baseline sample time")
+    ap.add_argument("--f1", action="store_true",
+                    help="also time the decode projections of the model leg's shapes: gdn_linear against cuBLAS "
+                         "(one GPU), and the row-parallel projection + sum over ranks fused (gdn_linear_allreduce, "
+                         "gdn_linear_push + gdn_pull_add_rmsnorm) against cuBLAS + peer all-reduce / NCCL (N > 1)")
     ap.add_argument("--no-model", action="store_true",
                     help="skip the config 3/4 model leg (the ~27B hybrid with random weights through the engine, "
                          "tensor-parallel over all ranks when launched with more than one)")
@@ -372,6 +376,16 @@ def load_traffic():
         return {}
 
 
+def measured_peaks():
+    """(HBM GB/s, bf16 TFLOP/s burst, source) from MEASURED_PEAKS.json, else the pool's fallback."""
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+        return peaks.get("hbm_gbs", 6650.0), peaks.get("bf16_tflops", 1590.0), "of measured"
+    except (OSError, ValueError):
+        return 6650.0, 1590.0, "of fallback"
+
+
 def run_ours(args, world, rank, local):
     ops = importlib.import_module(f"{PKG}.ops")
     peaks = {}
@@ -449,6 +463,8 @@ def run_ours(args, world, rank, local):
     if decode is not None:
         line["decode"] = decode
         line["gpu_launches"] += decode["gpu_launches"]
+    if args.f1:
+        line["f1"] = run_f1(world, rank)
     if not args.no_model:
         try:
             line["model"] = run_model(args, world, rank, local)
@@ -465,6 +481,115 @@ def run_ours(args, world, rank, local):
                                               "sample": dsample}
     if rank == 0:
         print(json.dumps(line), flush=True)
+
+
+def run_f1(world, rank, iters=64):
+    """Decode projections of the model leg (``model_slots(world)`` tokens, hidden 5,120) timed on the
+    device: CUDA graphs of ``iters`` calls, weights rotated through more than L2, max over ranks.
+    One GPU: gdn_linear vs cuBLAS for the TP-1 shapes, against the HBM roofline (weight bytes).
+    N > 1: per row-parallel shape (out_proj / o_proj k = 6,144 / N, down_proj k = 17,408 / N) the
+    fused projection + sum (gdn_linear_allreduce), its push / pull split with the residual add +
+    RMSNorm, and cuBLAS + peer all-reduce (+ gdn_add_rmsnorm) / cuBLAS + NCCL; the roofline target of a
+    fused call is the slower of its weight bytes over the HBM peak and the bytes it sends over NVLink
+    ((N - 1) x tokens x 5,120 x 2) over 770 GB/s per direction."""
+    ops = importlib.import_module(f"{PKG}.ops")
+    dev = torch.device("cuda", torch.cuda.current_device())
+    n = model_slots(world)
+    H = MODEL_TEXT_CONFIG["hidden_size"]
+    hbm = measured_peaks()[0]
+    out = {"tokens": n, "timing": "CUDA graph of %d calls, device time per call, max over ranks" % iters,
+           "hbm_peak_gbs": hbm, "nvlink_gbs": 770.0, "shapes": []}
+
+    def gtime(fn):
+        fn()
+        torch.cuda.synchronize()
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+        g = torch.cuda.CUDAGraph()
+        st = torch.cuda.Stream()
+        st.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(st):
+            with torch.cuda.graph(g, stream=st):
+                for _ in range(iters):
+                    fn()
+        torch.cuda.current_stream().wait_stream(st)
+        best = 1e30
+        for _ in range(3):
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            g.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            best = min(best, allreduce_max(e0.elapsed_time(e1) * 1e3 / iters, world))
+        del g
+        return best
+
+    def rotating(n_out, k):
+        copies = max(2, int(3e8 // (n_out * k * 2)) + 1)
+        Ws = [torch.randn(n_out, k, device=dev, dtype=torch.bfloat16) * 0.02 for _ in range(copies)]
+        it = iter(range(1 << 30))
+        return Ws, (lambda: Ws[next(it) % copies])
+
+    if world == 1:
+        shapes = [("o_proj / out_proj", H, 6144), ("down_proj", H, 17408), ("gate|up", 2 * 17408, H),
+                  ("GDN in_proj qkv|z|b|a", 16488, H), ("attention q|gate|k|v", 14336, H)]
+        for name, n_out, k in shapes:
+            Ws, nxt = rotating(n_out, k)
+            x = torch.randn(n, k, device=dev, dtype=torch.bfloat16)
+            y = torch.empty(n, n_out, device=dev, dtype=torch.bfloat16)
+            t_cub = gtime(lambda: torch.matmul(x, nxt().t(), out=y))
+            t_gdn = gtime(lambda: ops.linear(x, nxt(), out=y))
+            wb = n_out * k * 2
+            plan = ops.linear_plan(n, n_out, k)
+            out["shapes"].append({"name": name, "n_out": n_out, "k": k, "weight_bytes": wb, "splits": plan["splits"],
+                                  "gdn_linear_us": t_gdn, "cublas_us": t_cub,
+                                  "gdn_linear_hbm_frac": wb / (t_gdn * 1e-6) / 1e9 / hbm,
+                                  "cublas_hbm_frac": wb / (t_cub * 1e-6) / 1e9 / hbm})
+            del Ws
+        return out
+    tp_mod = importlib.import_module(f"{PKG}.tp")
+    import torch.distributed as dist
+    fl = tp_mod.PeerLinearAllReduce(n, H, dev)
+    ar = tp_mod.PeerAllReduce(n * H, dev)
+    nw = torch.ones(H, device=dev, dtype=torch.bfloat16)
+    try:
+        for name, k in (("o_proj / out_proj", 6144 // world), ("down_proj", 17408 // world)):
+            Ws, nxt = rotating(H, k)
+            x = torch.randn(n, k, device=dev, dtype=torch.bfloat16)
+            y = torch.empty(n, H, device=dev, dtype=torch.bfloat16)
+            res = torch.zeros(n, H, device=dev, dtype=torch.bfloat16)
+            nrm = torch.empty(n, H, device=dev, dtype=torch.bfloat16)
+
+            def cub_ar_norm():
+                torch.matmul(x, nxt().t(), out=y)
+                ar(y)
+                ops.add_rmsnorm(res, y, nw, 1e-6, out=nrm)
+
+            def push_pull():
+                fl.push(x, nxt())
+                fl.pull_add_rmsnorm(res, nw, 1e-6, out=nrm)
+
+            t = {"cublas": gtime(lambda: torch.matmul(x, nxt().t(), out=y)),
+                 "cublas_peer_allreduce": gtime(lambda: (torch.matmul(x, nxt().t(), out=y), ar(y))),
+                 "cublas_nccl": gtime(lambda: (torch.matmul(x, nxt().t(), out=y), dist.all_reduce(y))),
+                 "fused_gdn_linear_allreduce": gtime(lambda: fl(x, nxt())),
+                 "cublas_peer_allreduce_add_rmsnorm": gtime(cub_ar_norm),
+                 "push_pull_add_rmsnorm": gtime(push_pull)}
+            wb = H * k * 2
+            link = (world - 1) * n * H * 2
+            target = max(wb / (hbm * 1e9), link / 770e9) * 1e6
+            out["shapes"].append({"name": name, "n_out": H, "k": k, "weight_bytes_per_rank": wb,
+                                  "nvlink_bytes_out_per_rank": link, "roofline_target_us": target,
+                                  "splits_fused": ops.linear_plan(n, H, k, world=world)["splits"],
+                                  "splits_push": ops.linear_plan(n, H, k)["splits"],
+                                  "us": t, "fused_frac_of_roofline": target / t["fused_gdn_linear_allreduce"]})
+            del Ws
+    finally:
+        fl.close()
+        ar.close()
+    return out
 
 
 def model_slots(world):
