@@ -121,6 +121,12 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
+__device__ __forceinline__ uint32_t ld_relaxed_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
 __device__ __forceinline__ uint32_t* flag_at(char* buf, int p, int src, int g) {
   return reinterpret_cast<uint32_t*>(buf + kFlagOff) + (size_t(p) * kMaxWorld + src) * kMaxSegs + g;
 }
@@ -659,25 +665,28 @@ __global__ void __launch_bounds__(128) add_rmsnorm_kernel(const AddNormParams p)
   const int octs = p.dim / 8;
   char* own = PULL ? p.bufs[p.rank] : nullptr;
   if (PULL) {
-    // every rank's partial of every segment of the row must be here: wait (bounded) for the flags
+    // every rank's partial of every segment of the row must be here: poll all the row's flags with
+    // relaxed loads issued together (no ordering between them), round after round (bounded), then
+    // one system-scope fence orders the data reads after the flags
     if (tid == 0) s_ok = 1;
-    __syncthreads();
     const int nseg = (p.dim + kSegRows - 1) / kSegRows;
     const volatile int32_t* verr = p.err;
-    for (int idx = tid; idx < nseg * p.world; idx += 128) {
-      const int g = idx / p.world, src = idx - g * p.world;
-      const uint32_t e = reinterpret_cast<const uint32_t*>(own)[g];
-      const uint32_t* f = flag_at(own, int(e & 1u), src, g);
-      uint32_t it = 0;
-      while (ld_acquire_sys(f) != e) {
-        if (++it > p.spin_limit || (verr && *verr != 0)) {
-          s_ok = 0;
-          break;
-        }
-        __nanosleep(64);
+    for (uint32_t it = 0;; ++it) {
+      int mine = 1;
+      for (int idx = tid; idx < nseg * p.world; idx += 128) {
+        const int g = idx / p.world, src = idx - g * p.world;
+        const uint32_t e = reinterpret_cast<const uint32_t*>(own)[g];
+        mine &= ld_relaxed_sys(flag_at(own, int(e & 1u), src, g)) == e;
       }
-      if (!s_ok) break;
+      if (__syncthreads_and(mine)) break;
+      // give up together (block-uniform) when the limit is reached or another call already failed
+      if (__syncthreads_or(it > p.spin_limit || (verr && *verr != 0))) {
+        if (tid == 0) s_ok = 0;
+        break;
+      }
+      __nanosleep(64);
     }
+    fence_acq_rel_sys();
     __syncthreads();
     if (!s_ok) {  // a rank did not arrive: report it and leave x and out alone
       if (tid == 0 && p.err) atomicExch(p.err, 3);
@@ -749,6 +758,45 @@ __global__ void __launch_bounds__(128) add_rmsnorm_kernel(const AddNormParams p)
   }
 }
 
+// The push half of the exchange for a product computed elsewhere (a library GEMM): y [n, n_out]
+// bf16 goes, tile of 128 features by tile, into this rank's slot of every rank's exchange buffer,
+// with the same per-segment epochs, parity slots and flags as gdn_linear_push.  One CTA per tile.
+__global__ void __launch_bounds__(128) push_kernel(const __nv_bfloat16* __restrict__ y, int64_t y_rs, int n,
+                                                   int n_out, const Params p) {
+  __shared__ uint32_t s_epoch[kSegs];
+  const int tid = threadIdx.x, mt = blockIdx.x;
+  const int gseg0 = mt * kSegs;
+  const int segs_total = (n_out + kSegRows - 1) / kSegRows;
+  const int nseg = segs_total - gseg0 < kSegs ? segs_total - gseg0 : kSegs;
+  char* own = p.bufs[p.rank];
+  if (tid < nseg) {
+    uint32_t* ep = reinterpret_cast<uint32_t*>(own) + gseg0 + tid;
+    const uint32_t e = *ep + 1;
+    *ep = e;
+    s_epoch[tid] = e;
+  }
+  __syncthreads();
+  const int nvec = 2 * nseg * n;  // (8-feature group, token) vectors, token fastest
+  for (int v = tid; v < nvec; v += 128) {
+    const int o = v / n, j = v - o * n;
+    const int f = mt * kBM + o * 8;
+    if (f >= n_out) continue;
+    const uint4 val = *reinterpret_cast<const uint4*>(y + int64_t(j) * y_rs + f);
+    const int par = int(s_epoch[o >> 1] & 1u);
+#pragma unroll
+    for (int r = 0; r < kMaxWorld; ++r) {
+      if (r >= p.world) break;
+      reinterpret_cast<uint4*>(p.bufs[r] + kDataOff)[((int64_t(par) * p.world + p.rank) * p.max_octs + f / 8) *
+                                                     p.max_rows + j] = val;
+    }
+  }
+  __syncthreads();  // every thread's stores before the flag threads' system-scope release
+  if (tid < nseg * p.world) {
+    const int sg = tid / p.world, dst = tid - sg * p.world;
+    st_release_sys(flag_at(p.bufs[dst], int(s_epoch[sg] & 1u), p.rank, gseg0 + sg), s_epoch[sg]);
+  }
+}
+
 static int check_add_norm(const void* x, int64_t x_rs, const void* w, const void* out, int64_t out_rs, int64_t rows,
                           int dim, int dtype, const char* what) {
   if (dtype != GDN_BF16) return fail(GDN_ERR_DTYPE, "%s: dtype %d (bf16 only)", what, dtype);
@@ -809,6 +857,30 @@ extern "C" int gdn_linear_push(const void* x, int64_t x_rs, const void* w, int64
   // y is not written in push mode; x stands in as a valid, aligned pointer for the argument checks
   return lin::launch(x, x_rs, w, w_rs, const_cast<void*>(x), n_out, n, n_out, k, splits, prm, as_stream(stream),
                      "gdn_linear_push");
+}
+
+extern "C" int gdn_push_partial(const void* y, int64_t y_rs, int n, int n_out, int rank, int world,
+                                void* const* bufs, int max_rows, int max_out, int dtype, void* stream) {
+  if (dtype != GDN_BF16) return fail(GDN_ERR_DTYPE, "gdn_push_partial: dtype %d (bf16 only)", dtype);
+  if (world < 2 || world > lin::kMaxWorld || rank < 0 || rank >= world || !bufs)
+    return fail(GDN_ERR_ARG, "gdn_push_partial: rank %d of %d (world 2..%d)", rank, world, lin::kMaxWorld);
+  if (n < 1 || n_out < 8 || n_out % 8 || n > max_rows || n_out > max_out || max_out % 8 ||
+      max_out > lin::kMaxSegs * lin::kSegRows || max_rows > lin::kMaxTokens)
+    return fail(GDN_ERR_ARG, "gdn_push_partial: %d x %d does not fit the buffers (max_rows %d, max_out %d)", n, n_out,
+                max_rows, max_out);
+  if (!y || !aligned(y, 16) || y_rs % 8 || y_rs < n_out) return fail(GDN_ERR_ARG, "gdn_push_partial: y rows");
+  lin::Params prm{};
+  prm.rank = rank;
+  prm.world = world;
+  prm.max_rows = max_rows;
+  prm.max_octs = max_out / 8;
+  for (int r = 0; r < world; ++r) {
+    if (!bufs[r] || !aligned(bufs[r], 16)) return fail(GDN_ERR_ARG, "gdn_push_partial: buffer %d", r);
+    prm.bufs[r] = static_cast<char*>(bufs[r]);
+  }
+  lin::push_kernel<<<unsigned((n_out + lin::kBM - 1) / lin::kBM), 128, 0, as_stream(stream)>>>(
+      static_cast<const __nv_bfloat16*>(y), y_rs, n, n_out, prm);
+  return check_launch("gdn_push_partial");
 }
 
 extern "C" int gdn_pull_add_rmsnorm(void* x, int64_t x_rs, const void* weight, void* out, int64_t out_rs, int64_t rows,

@@ -128,6 +128,7 @@ class CBEngine:
         self.graph_decode = graph_decode
         if not hasattr(self, "peer_linear"):
             self.peer_linear = None       # TPEngine sets its tensor-parallel exchange before this runs
+            self.decode_sum = None
         self._graphs, self._graph_out = {}, {}
         if graph_decode:
             self._capture_graphs()
@@ -225,14 +226,18 @@ class CBEngine:
         """A layer's output projection, the residual add and the next RMSNorm of the decode step:
         x <- x + proj(a) in place; returns norm(x).  With a tensor-parallel exchange (``peer_linear``,
         set by TPEngine) the projection pushes this rank's partial to every rank (gdn_linear_push)
-        and one kernel sums the ranks' partials, adds and normalizes (gdn_pull_add_rmsnorm);
+        (gdn_linear_push, or a cuBLAS GEMM and gdn_push_partial) and one kernel sums the ranks'
+        partials, adds and normalizes (gdn_pull_add_rmsnorm);
         otherwise the projection's own forward (cuBLAS, plus the all-reduce of AllReduceLinear under
         TP) is followed by gdn_add_rmsnorm.  Both equal the reference's ``x = x + proj(a)`` and the
         norm module of the next step (src/cb_engine.py:295-355)."""
         ex = self.peer_linear
         lin = getattr(proj, "lin", None)
         if ex is not None and lin is not None and lin.bias is None and ex.applies(a, lin.weight):
-            ex.push(a, lin.weight)
+            if self.decode_sum == "fused":
+                ex.push(a, lin.weight)                   # tcgen05 projection sending its tiles
+            else:
+                ex.push_partial(F.linear(a, lin.weight))  # cuBLAS projection, then the push
             return ex.pull_add_rmsnorm(x, norm.weight, norm.eps)
         return ops.add_rmsnorm(x, proj(a), norm.weight, norm.eps)
 

@@ -122,6 +122,7 @@ class PeerLinearAllReduce(_PeerBuffers):
         nbytes = _lib.load().gdn_linear_ar_buffer_bytes(dist.get_world_size(), self.max_rows, self.max_out,
                                                         _lib.GDN_BF16)
         super().__init__(nbytes, device, "PeerLinearAllReduce")
+        self.route_linear = True   # AllReduceLinear.forward may run gdn_linear_allreduce through it
 
     def applies(self, x, weight):
         """Whether this projection goes through the fused kernel (depends only on shapes and dtypes,
@@ -151,6 +152,16 @@ class PeerLinearAllReduce(_PeerBuffers):
                                             int(splits), self.rank, self.world, self._table, self.max_rows,
                                             self.max_out, self.err.data_ptr(), _lib.GDN_BF16,
                                             torch.cuda.current_stream().cuda_stream), "gdn_linear_push")
+
+    def push_partial(self, y):
+        """First half for a product computed elsewhere: this rank's partial y [rows, n_out] bf16 goes to
+        every rank (gdn_push_partial).  Must be followed by ``pull_add_rmsnorm`` of the same shape."""
+        y2 = y.reshape(-1, y.shape[-1])
+        if y2.stride(-1) != 1 or y2.stride(0) % 8 or y2.data_ptr() % 16:
+            y2 = y2.contiguous()
+        _lib.check(self.lib.gdn_push_partial(y2.data_ptr(), y2.stride(0), y2.shape[0], y2.shape[1], self.rank,
+                                             self.world, self._table, self.max_rows, self.max_out, _lib.GDN_BF16,
+                                             torch.cuda.current_stream().cuda_stream), "gdn_push_partial")
 
     def pull_add_rmsnorm(self, x, weight, eps, out=None):
         """Second half: h = the sum over ranks of the pushed partials; x <- bf16(x + h) IN PLACE;
@@ -221,7 +232,7 @@ class AllReduceLinear(nn.Module):
 
     def forward(self, x):
         fused = _PEER_LINEAR
-        if fused is not None and self.lin.bias is None and fused.applies(x, self.lin.weight):
+        if fused is not None and fused.route_linear and self.lin.bias is None and fused.applies(x, self.lin.weight):
             return fused(x, self.lin.weight)
         partial = self.lin(x)
         reducer = _PEER_AR
@@ -420,23 +431,38 @@ def init_tp(rank, world, backend="nccl", master_port="29561", timeout_s=120):
 
 
 class TPEngine(CBEngine):
-    """CBEngine on sharded weights (src/cb_tp.py:117-285).  With ``fused_linear`` the decode
-    steps' row-parallel projections run as one kernel each that also sums over the ranks
-    (PeerLinearAllReduce); with ``peer_allreduce`` (default) decode-sized sums the fused kernel does
-    not take go through PeerAllReduce after a cuBLAS GEMM; prefill's larger ones through F.linear +
-    NCCL.
-    Decode graphs capture whichever runs, and every rank captures the same sequence of graphs.
-    ``close()`` (collective) releases the graphs and the peer buffers."""
+    """CBEngine on sharded weights (src/cb_tp.py:117-285).  ``decode_sum`` picks how a decode step's
+    row-parallel projections (o_proj, out_proj, down_proj) are summed over the ranks:
+      * "push" (default): cuBLAS GEMM, its partial pushed to every rank (gdn_push_partial), and the
+        following residual add + RMSNorm summing the ranks (gdn_pull_add_rmsnorm);
+      * "fused": the same with the projection itself on this library's tensor cores sending its
+        tiles as they finish (gdn_linear_push);
+      * "peer": cuBLAS GEMM, peer-memory all-reduce (gdn_allreduce), gdn_add_rmsnorm;
+      * "nccl": F.linear + NCCL all-reduce (the reference's AllReduceLinear).
+    Prefill's larger sums go through F.linear + NCCL.  Decode graphs capture whichever runs, and
+    every rank captures the same sequence of graphs.  ``close()`` (collective) releases the graphs
+    and the peer buffers.  (``peer_allreduce=False`` / ``fused_linear=True`` are the older switches
+    for "nccl" / "fused".)"""
 
-    def __init__(self, model, n_slots, t_max, device, tp, graph_decode=False, peer_allreduce=True,
-                 fused_linear=False):
+    def __init__(self, model, n_slots, t_max, device, tp, graph_decode=False, decode_sum="push",
+                 peer_allreduce=None, fused_linear=None):
+        if fused_linear:
+            decode_sum = "fused"
+        elif peer_allreduce is False:
+            decode_sum = "nccl"
+        if decode_sum not in ("push", "fused", "peer", "nccl"):
+            raise ValueError(f"decode_sum {decode_sum!r}")
+        self.decode_sum = decode_sum
         self.peer_ar = self.peer_linear = None
         if tp > 1:
             hidden = model.config.text_config.hidden_size
-            if peer_allreduce:
+            if decode_sum != "nccl":
                 self.peer_ar = enable_peer_allreduce(n_slots * hidden, device)
-            if fused_linear:
+            if decode_sum in ("push", "fused"):
                 self.peer_linear = enable_peer_linear(n_slots, hidden, device)
+                # outside the decode step's projection + norm pairs, AllReduceLinear runs the fused
+                # projection + sum only in "fused" mode
+                self.peer_linear.route_linear = decode_sum == "fused"
         super().__init__(model, n_slots, t_max, device, graph_decode=graph_decode, tp=tp)
 
     def check_errors(self):

@@ -95,10 +95,11 @@ def parse():
                     help="after the model leg, profile graph-replayed decode steps (torch.profiler, device time "
                          "per kernel) and report a per-category breakdown")
     ap.add_argument("--model-gen", type=int, default=512, help="greedy tokens per turn of the model leg")
-    ap.add_argument("--model-allreduce", choices=["fused", "peer", "nccl"], default="peer",
-                    help="TP decode sums: the row-parallel projection pushing its partial to every rank and the "
-                         "residual add + RMSNorm summing them (gdn_linear_push + gdn_pull_add_rmsnorm), cuBLAS + "
-                         "this library's peer-memory all-reduce, or cuBLAS + NCCL")
+    ap.add_argument("--model-allreduce", choices=["push", "fused", "peer", "nccl"], default="push",
+                    help="TP decode sums (TPEngine decode_sum): cuBLAS + push of the partial + residual add / RMSNorm "
+                         "summing the ranks (gdn_push_partial + gdn_pull_add_rmsnorm); the same with the tcgen05 "
+                         "projection pushing its tiles (gdn_linear_push); cuBLAS + peer-memory all-reduce; or "
+                         "cuBLAS + NCCL")
     return ap.parse_args()
 
 
@@ -571,12 +572,18 @@ def run_f1(world, rank, iters=64):
                 fl.push(x, nxt())
                 fl.pull_add_rmsnorm(res, nw, 1e-6, out=nrm)
 
+            def cub_push_pull():
+                torch.matmul(x, nxt().t(), out=y)
+                fl.push_partial(y)
+                fl.pull_add_rmsnorm(res, nw, 1e-6, out=nrm)
+
             t = {"cublas": gtime(lambda: torch.matmul(x, nxt().t(), out=y)),
                  "cublas_peer_allreduce": gtime(lambda: (torch.matmul(x, nxt().t(), out=y), ar(y))),
                  "cublas_nccl": gtime(lambda: (torch.matmul(x, nxt().t(), out=y), dist.all_reduce(y))),
                  "fused_gdn_linear_allreduce": gtime(lambda: fl(x, nxt())),
                  "cublas_peer_allreduce_add_rmsnorm": gtime(cub_ar_norm),
-                 "push_pull_add_rmsnorm": gtime(push_pull)}
+                 "push_pull_add_rmsnorm": gtime(push_pull),
+                 "cublas_push_pull_add_rmsnorm": gtime(cub_push_pull)}
             wb = H * k * 2
             link = (world - 1) * n * H * 2
             target = max(wb / (hbm * 1e9), link / 770e9) * 1e6
@@ -823,9 +830,8 @@ def run_model(args, world, rank, local):
     reqs = serve.synthetic_requests(n_req, MODEL_TEXT_CONFIG["vocab_size"], seed=4321, max_turns=args.model_turns)
     bucket = eng_mod.GRAPH_BUCKET
     t_max = -(-(serve.max_context(reqs, args.model_gen) + 1) // bucket) * bucket
-    peer = args.model_allreduce in ("peer", "fused")
-    eng = (tp_mod.TPEngine(model, slots, t_max, dev, world, graph_decode=True, peer_allreduce=peer,
-                           fused_linear=args.model_allreduce == "fused") if world > 1
+    eng = (tp_mod.TPEngine(model, slots, t_max, dev, world, graph_decode=True, decode_sum=args.model_allreduce)
+           if world > 1
            else eng_mod.CBEngine(model, slots, t_max, dev, graph_decode=True))
     build_s = time.time() - t_build
     # warm-up: single-turn requests of the same prompt lengths through the same loop (GEMM shapes,
@@ -886,10 +892,11 @@ def run_model(args, world, rank, local):
                                              "algebra + causal attention; slowest rank"}},
            "timing": "wall clock per engine call (each ends with its host read of the tokens), max over ranks",
            "graph": True, "weights": "random-init bf16",
-           "allreduce": ("none" if world <= 1 else
-                         "gdn_linear_push + gdn_pull_add_rmsnorm (peer memory) for decode, NCCL for prefill"
-                         if args.model_allreduce == "fused" else
-                         "gdn_allreduce (peer memory) for decode, NCCL for prefill" if peer else "NCCL"),
+           "allreduce": ("none" if world <= 1 else {
+               "push": "cuBLAS + gdn_push_partial + gdn_pull_add_rmsnorm (peer memory) for decode, NCCL for prefill",
+               "fused": "gdn_linear_push + gdn_pull_add_rmsnorm (peer memory) for decode, NCCL for prefill",
+               "peer": "cuBLAS + gdn_allreduce (peer memory) for decode, NCCL for prefill",
+               "nccl": "NCCL"}[args.model_allreduce]),
            "lm_head": "vocabulary-parallel" if world > 1 else "full", "build_s": build_s}
     if parity is not None:
         out["tp_parity"] = parity

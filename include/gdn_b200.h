@@ -392,6 +392,10 @@ GDN_API int gdn_linear_allreduce(const void* x, int64_t x_rs, const void* w, int
 GDN_API int gdn_linear_push(const void* x, int64_t x_rs, const void* w, int64_t w_rs, int n, int n_out, int k,
                             int splits, int rank, int world, void* const* bufs, int max_rows, int max_out,
                             int32_t* err_flag, int dtype, void* stream);
+/* gdn_push_partial: the push of gdn_linear_push for a product y [n, n_out]
+ * computed elsewhere (e.g. a library GEMM), same buffers, epochs and flags. */
+GDN_API int gdn_push_partial(const void* y, int64_t y_rs, int n, int n_out, int rank, int world, void* const* bufs,
+                             int max_rows, int max_out, int dtype, void* stream);
 GDN_API int gdn_pull_add_rmsnorm(void* x, int64_t x_rs, const void* weight, void* out, int64_t out_rs, int64_t rows,
                                  int dim, float eps, int rank, int world, void* const* bufs, int max_rows,
                                  int max_out, uint32_t spin_limit, int32_t* err_flag, int dtype, void* stream);

@@ -9,8 +9,8 @@ bf16(sum over r of fp32(gdn_linear(x_r, W_r)))
 call to call (the per-segment epochs and the double-buffered slots must stay in step; outputs
 narrower than the buffers; 1-128 tokens), the calls are also captured in a CUDA graph and replayed
 with fresh inputs, and the result is compared with F.linear + NCCL all-reduce within bf16
-tolerance.  The push / pull split (gdn_linear_push, then gdn_pull_add_rmsnorm summing the ranks,
-adding the residual and normalizing) must equal the all-reduce output added to the residual in bf16
+tolerance.  The push / pull split (gdn_linear_push, or a cuBLAS product pushed by gdn_push_partial,
+then gdn_pull_add_rmsnorm summing the ranks, adding the residual and normalizing) must equal the all-reduce output added to the residual in bf16
 and ops.rmsnorm BIT FOR BIT, eagerly, mixed with full fused calls, and captured in a graph.  A second
 instance with a short spin limit checks the failure path: only rank 0 calls, its waits run out (in
 the fused call, and in the pull after a push), it reports error 3 and leaves y / x / out unwritten,
@@ -126,6 +126,19 @@ def _rank(rank, world, port, q):
                 ok &= torch.equal(res, ref_x) and torch.equal(got, ref_out)
                 if case == 1:                # a full fused call between push/pull pairs
                     ok &= torch.equal(fl(x, w), expected(x, w))
+                # the push of a product computed elsewhere (cuBLAS): the sum of the ranks' cuBLAS partials
+                part = torch.nn.functional.linear(x, w)
+                parts = [torch.empty_like(part) for _ in range(world)]
+                dist.all_gather(parts, part)
+                acc = torch.zeros(part.shape, dtype=torch.float32, device=dev)
+                for pp in parts:
+                    acc += pp.float()
+                res2 = (torch.randn(n, HIDDEN, generator=torch.Generator().manual_seed(91 + case)) * 2).to(
+                    torch.bfloat16).to(dev)
+                ref2_x = res2 + acc.to(torch.bfloat16)
+                fl.push_partial(part)
+                got2 = fl.pull_add_rmsnorm(res2, nw, 1e-6)
+                ok &= torch.equal(res2, ref2_x) and torch.equal(got2, ops.rmsnorm(ref2_x, nw, 1e-6))
         out["push_pull"] = bool(ok)
         # push / pull captured in a graph (two pairs), replayed with fresh inputs
         pshapes = [CASES[0], CASES[1]]
