@@ -66,6 +66,9 @@ SIGNATURES = {
                                     _i32, _i32, C.c_uint32, _vp, _i32, _vp]),
     "gdn_linear_push": (_i32, [_vp, _i64, _vp, _i64, _i32, _i32, _i32, _i32, _i32, _i32, _vp, _i32, _i32, _vp,
                                _i32, _vp]),
+    "gdn_ar_norm_buffer_bytes": (_sz, [_i32, _i32, _i32, _i32]),
+    "gdn_allreduce_add_rmsnorm": (_i32, [_vp, _i64, _vp, _i64, _vp, _vp, _i64, _i64, _i32, _f32, _i32, _i32, _vp,
+                                         _i32, C.c_uint32, _vp, _i32, _vp]),
     "gdn_push_partial": (_i32, [_vp, _i64, _i32, _i32, _i32, _i32, _vp, _i32, _i32, _i32, _vp]),
     "gdn_pull_add_rmsnorm": (_i32, [_vp, _i64, _vp, _vp, _i64, _i64, _i32, _f32, _i32, _i32, _vp, _i32, _i32,
                                     C.c_uint32, _vp, _i32, _vp]),

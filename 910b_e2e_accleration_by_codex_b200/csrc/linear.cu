@@ -913,3 +913,164 @@ extern "C" int gdn_pull_add_rmsnorm(void* x, int64_t x_rs, const void* weight, v
   lin::add_rmsnorm_kernel<true><<<unsigned(rows), 128, 0, as_stream(stream)>>>(p);
   return check_launch("gdn_pull_add_rmsnorm");
 }
+
+// ---------------------------------------------------------------------------------------------
+// All-reduce fused into its consumer: the row-parallel projection's sum over ranks, the residual
+// add and the next RMSNorm (AllReduceLinear's dist.all_reduce, x + h and Qwen3_5RMSNorm,
+// src/cb_tp.py:25-35, src/cb_engine.py:295-355) in one kernel, one CTA per token row:
+//   1. this rank's partial row y[j] goes into its slot of every rank's buffer (plain 16-byte stores
+//      over NVLink), then one flag per (row, destination) is raised with a system-scope release;
+//   2. the row's flags from every other rank are polled (relaxed loads, bounded, block-uniform
+//      give-up) and one system-scope fence orders the reads after them;
+//   3. h = bf16(sum of the ranks' partials in rank order, fp32); x[j] = bf16(x[j] + h) in place;
+//      out[j] = bf16(x[j] * rsqrt(mean(x[j]^2) + eps) * (1 + w)) with gdn_rmsnorm's arithmetic,
+// bit for bit gdn_allreduce -> x + h -> gdn_rmsnorm.  Buffer of one rank:
+//   [0, 1 KiB) epoch[kMaxTokens]; [1 KiB, 1 KiB + 16 KiB) flag[2][kMaxWorld][kMaxTokens];
+//   [kArDataOff, ...) data[2][world][max_rows][dim] bf16 (dim fixed for the buffer's lifetime).
+// The epoch of row j counts the calls that touched it, identically on every rank; parity
+// double-buffers the data as in the exchange above.
+namespace gdn {
+namespace lin {
+
+constexpr size_t kArFlagOff = 1024;
+constexpr size_t kArDataOff = kArFlagOff + size_t(2) * kMaxWorld * kMaxTokens * 4;
+static_assert(kMaxTokens * 4 <= kArFlagOff, "row epochs");
+
+__device__ __forceinline__ uint32_t* arflag_at(char* buf, int p, int src, int j) {
+  return reinterpret_cast<uint32_t*>(buf + kArFlagOff) + (size_t(p) * kMaxWorld + src) * kMaxTokens + j;
+}
+
+__global__ void __launch_bounds__(128) ar_add_rmsnorm_kernel(const AddNormParams p) {
+  constexpr int NV = 8192 / (128 * 8);
+  __shared__ float red[4];
+  __shared__ uint32_t s_e;
+  __shared__ int s_ok;
+  const int tid = threadIdx.x, j = blockIdx.x;
+  const int octs = p.dim / 8;
+  char* own = p.bufs[p.rank];
+  if (tid == 0) {
+    uint32_t* ep = reinterpret_cast<uint32_t*>(own) + j;
+    s_e = *ep + 1;
+    *ep = s_e;
+    s_ok = 1;
+  }
+  __syncthreads();
+  const uint32_t e = s_e;
+  const int par = int(e & 1u);
+  auto slot = [&](char* buf, int src) {
+    return reinterpret_cast<uint4*>(buf + kArDataOff) + ((int64_t(par) * p.world + src) * p.max_rows + j) * octs;
+  };
+  __nv_bfloat16* xr = p.x + int64_t(j) * p.x_rs;
+  uint4 hu[NV], xu[NV], wu[NV];
+#pragma unroll
+  for (int v = 0; v < NV; ++v) {
+    const int o = v * 128 + tid;
+    if (o < octs) {
+      hu[v] = *reinterpret_cast<const uint4*>(p.h + int64_t(j) * p.h_rs + o * 8);
+      xu[v] = *reinterpret_cast<const uint4*>(xr + o * 8);
+      wu[v] = *reinterpret_cast<const uint4*>(p.w + o * 8);
+#pragma unroll
+      for (int r = 0; r < kMaxWorld; ++r) {
+        if (r >= p.world) break;
+        if (r != p.rank) slot(p.bufs[r], p.rank)[o] = hu[v];
+      }
+    }
+  }
+  __syncthreads();  // every thread's stores before the flag threads' system-scope release
+  if (tid < p.world && tid != p.rank) st_release_sys(arflag_at(p.bufs[tid], par, p.rank, j), e);
+  const volatile int32_t* verr = p.err;
+  for (uint32_t it = 0;; ++it) {
+    const int mine = tid >= p.world || tid == p.rank || ld_relaxed_sys(arflag_at(own, par, tid, j)) == e;
+    if (__syncthreads_and(mine)) break;
+    if (__syncthreads_or(it > p.spin_limit || (verr && *verr != 0))) {
+      if (tid == 0) s_ok = 0;
+      break;
+    }
+    __nanosleep(32);
+  }
+  fence_acq_rel_sys();
+  __syncthreads();
+  if (!s_ok) {  // a rank did not arrive: report it and leave x and out alone
+    if (tid == 0 && p.err) atomicExch(p.err, 3);
+    return;
+  }
+  float xv[NV][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int v = 0; v < NV; ++v) {
+    const int o = v * 128 + tid;
+    if (o < octs) {
+      float hv[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      for (int src = 0; src < p.world; ++src) add8(src == p.rank ? hu[v] : slot(own, src)[o], hv);
+      float xin[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      add8(xu[v], xin);
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        xv[v][i] = __bfloat162float(__float2bfloat16_rn(xin[i] + __bfloat162float(__float2bfloat16_rn(hv[i]))));
+      *reinterpret_cast<uint4*>(xr + o * 8) = pack8(xv[v]);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ss += xv[v][i] * xv[v][i];
+    }
+  }
+  ss = warp_sum(ss);
+  if ((tid & 31) == 0) red[tid >> 5] = ss;
+  __syncthreads();
+  const float r = 1.0f / sqrtf((red[0] + red[1] + red[2] + red[3]) / float(p.dim) + p.eps);
+  __nv_bfloat16* yr = p.out + int64_t(j) * p.out_rs;
+#pragma unroll
+  for (int v = 0; v < NV; ++v) {
+    const int o = v * 128 + tid;
+    if (o < octs) {
+      float wv[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      add8(wu[v], wv);
+      float y[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) y[i] = (xv[v][i] * r) * (1.0f + wv[i]);
+      *reinterpret_cast<uint4*>(yr + o * 8) = pack8(y);
+    }
+  }
+}
+
+}  // namespace lin
+}  // namespace gdn
+
+extern "C" size_t gdn_ar_norm_buffer_bytes(int world, int max_rows, int dim, int dtype) {
+  if (world < 1 || world > lin::kMaxWorld || dtype != GDN_BF16 || max_rows < 1 || max_rows > lin::kMaxTokens ||
+      dim < 8 || dim > 8192 || dim % 8)
+    return 0;
+  return lin::kArDataOff + 2 * size_t(world) * size_t(max_rows) * size_t(dim) * 2;
+}
+
+extern "C" int gdn_allreduce_add_rmsnorm(void* x, int64_t x_rs, const void* h, int64_t h_rs, const void* weight,
+                                         void* out, int64_t out_rs, int64_t rows, int dim, float eps, int rank,
+                                         int world, void* const* bufs, int max_rows, uint32_t spin_limit,
+                                         int32_t* err_flag, int dtype, void* stream) {
+  int rc = lin::check_add_norm(x, x_rs, weight, out, out_rs, rows, dim, dtype, "gdn_allreduce_add_rmsnorm");
+  if (rc) return rc;
+  if (!h || !aligned(h, 16) || h_rs % 8 || h_rs < dim) return fail(GDN_ERR_ARG, "gdn_allreduce_add_rmsnorm: h rows");
+  if (world < 2 || world > lin::kMaxWorld || rank < 0 || rank >= world || !bufs)
+    return fail(GDN_ERR_ARG, "gdn_allreduce_add_rmsnorm: rank %d of %d (world 2..%d)", rank, world, lin::kMaxWorld);
+  if (rows > max_rows || max_rows > lin::kMaxTokens)
+    return fail(GDN_ERR_ARG, "gdn_allreduce_add_rmsnorm: %lld rows > buffer rows %d", (long long)rows, max_rows);
+  lin::AddNormParams p{};
+  p.x = static_cast<__nv_bfloat16*>(x);
+  p.x_rs = x_rs;
+  p.h = static_cast<const __nv_bfloat16*>(h);
+  p.h_rs = h_rs;
+  p.w = static_cast<const __nv_bfloat16*>(weight);
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.out_rs = out_rs;
+  p.dim = dim;
+  p.eps = eps;
+  p.rank = rank;
+  p.world = world;
+  p.max_rows = max_rows;
+  p.spin_limit = spin_limit ? spin_limit : (1u << 22);
+  p.err = err_flag;
+  for (int r = 0; r < world; ++r) {
+    if (!bufs[r] || !aligned(bufs[r], 16)) return fail(GDN_ERR_ARG, "gdn_allreduce_add_rmsnorm: buffer %d", r);
+    p.bufs[r] = static_cast<char*>(bufs[r]);
+  }
+  lin::ar_add_rmsnorm_kernel<<<unsigned(rows), 128, 0, as_stream(stream)>>>(p);
+  return check_launch("gdn_allreduce_add_rmsnorm");
+}

@@ -127,7 +127,8 @@ class CBEngine:
         self._err = torch.zeros(1, dtype=torch.int32, device=self.dev)
         self.graph_decode = graph_decode
         if not hasattr(self, "peer_linear"):
-            self.peer_linear = None       # TPEngine sets its tensor-parallel exchange before this runs
+            self.peer_linear = None       # TPEngine sets its tensor-parallel exchanges before this runs
+            self.peer_norm = None
             self.decode_sum = None
         self._graphs, self._graph_out = {}, {}
         if graph_decode:
@@ -225,14 +226,21 @@ class CBEngine:
     def _proj_add_norm(self, proj, a, x, norm):
         """A layer's output projection, the residual add and the next RMSNorm of the decode step:
         x <- x + proj(a) in place; returns norm(x).  With a tensor-parallel exchange (``peer_linear``,
-        set by TPEngine) the projection pushes this rank's partial to every rank (gdn_linear_push)
+        set by TPEngine) the sum over ranks runs inside the add + norm kernel
+        (gdn_allreduce_add_rmsnorm), or the projection pushes this rank's partial to every rank (gdn_linear_push)
         (gdn_linear_push, or a cuBLAS GEMM and gdn_push_partial) and one kernel sums the ranks'
         partials, adds and normalizes (gdn_pull_add_rmsnorm);
         otherwise the projection's own forward (cuBLAS, plus the all-reduce of AllReduceLinear under
         TP) is followed by gdn_add_rmsnorm.  Both equal the reference's ``x = x + proj(a)`` and the
         norm module of the next step (src/cb_engine.py:295-355)."""
-        ex = self.peer_linear
         lin = getattr(proj, "lin", None)
+        arn = self.peer_norm
+        if arn is not None and lin is not None and lin.bias is None:
+            h = F.linear(a, lin.weight)                   # this rank's partial (cuBLAS)
+            if arn.applies(h):
+                return arn(x, h, norm.weight, norm.eps)   # sum over ranks + add + norm, one kernel
+            return ops.add_rmsnorm(x, proj.reduce(h), norm.weight, norm.eps)
+        ex = self.peer_linear
         if ex is not None and lin is not None and lin.bias is None and ex.applies(a, lin.weight):
             if self.decode_sum == "fused":
                 ex.push(a, lin.weight)                   # tcgen05 projection sending its tiles

@@ -108,6 +108,40 @@ class PeerAllReduce(_PeerBuffers):
         return y
 
 
+class PeerAllReduceAddNorm(_PeerBuffers):
+    """The all-reduce of a row-parallel projection fused into its consumer
+    (gdn_allreduce_add_rmsnorm): ``self(x, h, weight, eps)`` sums this rank's partial ``h``
+    [rows, dim] over the ranks, adds it to the residual ``x`` in place and returns RMSNorm(x), one
+    kernel with one NVLink round trip per token row; bit for bit PeerAllReduce, then x + h, then
+    ops.rmsnorm.  Collective like PeerAllReduce (same calls, same shapes on every rank; a rank that
+    does not arrive makes the others set ``err`` to 3)."""
+
+    def __init__(self, max_rows, dim, device, spin_limit=0):
+        self.max_rows, self.dim = int(max_rows), int(dim)
+        self.spin_limit = int(spin_limit)
+        nbytes = _lib.load().gdn_ar_norm_buffer_bytes(dist.get_world_size(), self.max_rows, self.dim, _lib.GDN_BF16)
+        super().__init__(nbytes, device, "PeerAllReduceAddNorm")
+
+    def applies(self, h):
+        return (not self.closed and h.dtype == torch.bfloat16 and h.shape[-1] == self.dim
+                and h.numel() // self.dim <= self.max_rows)
+
+    def __call__(self, x, h, weight, eps, out=None):
+        dim = self.dim
+        x2, h2 = x.view(-1, dim), h.reshape(-1, dim)
+        if h2.stride(-1) != 1 or h2.stride(0) % 8 or h2.data_ptr() % 16:
+            h2 = h2.contiguous()
+        w = weight.to(x.dtype).contiguous()
+        y = torch.empty(x2.shape, dtype=x.dtype, device=x.device) if out is None else out.view(-1, dim)
+        _lib.check(self.lib.gdn_allreduce_add_rmsnorm(x2.data_ptr(), x2.stride(0), h2.data_ptr(), h2.stride(0),
+                                                      w.data_ptr(), y.data_ptr(), y.stride(0), x2.shape[0], dim,
+                                                      float(eps), self.rank, self.world, self._table, self.max_rows,
+                                                      self.spin_limit, self.err.data_ptr(), _lib.GDN_BF16,
+                                                      torch.cuda.current_stream().cuda_stream),
+                   "gdn_allreduce_add_rmsnorm")
+        return y.view(x.shape)
+
+
 class PeerLinearAllReduce(_PeerBuffers):
     """A row-parallel projection and its sum over the ranks in one kernel (gdn_linear_allreduce):
     ``self(x, weight)`` = sum over ranks of x_r weight_r^T, for up to ``max_rows`` tokens and
@@ -234,7 +268,12 @@ class AllReduceLinear(nn.Module):
         fused = _PEER_LINEAR
         if fused is not None and fused.route_linear and self.lin.bias is None and fused.applies(x, self.lin.weight):
             return fused(x, self.lin.weight)
-        partial = self.lin(x)
+        return self.reduce(self.lin(x))
+
+    @staticmethod
+    def reduce(partial):
+        """Sum this rank's partial over the ranks in place (peer-memory kernel when one is enabled
+        and the size fits, else NCCL); returns it."""
         reducer = _PEER_AR
         if reducer is None or not reducer.applies(partial):
             dist.all_reduce(partial)
@@ -433,7 +472,9 @@ def init_tp(rank, world, backend="nccl", master_port="29561", timeout_s=120):
 class TPEngine(CBEngine):
     """CBEngine on sharded weights (src/cb_tp.py:117-285).  ``decode_sum`` picks how a decode step's
     row-parallel projections (o_proj, out_proj, down_proj) are summed over the ranks:
-      * "push" (default): cuBLAS GEMM, its partial pushed to every rank (gdn_push_partial), and the
+      * "arnorm" (default): cuBLAS GEMM, then one kernel per token row that sums the partials over
+        the ranks, adds the residual and applies the next RMSNorm (gdn_allreduce_add_rmsnorm);
+      * "push": cuBLAS GEMM, its partial pushed to every rank (gdn_push_partial), and the
         following residual add + RMSNorm summing the ranks (gdn_pull_add_rmsnorm);
       * "fused": the same with the projection itself on this library's tensor cores sending its
         tiles as they finish (gdn_linear_push);
@@ -444,20 +485,22 @@ class TPEngine(CBEngine):
     and the peer buffers.  (``peer_allreduce=False`` / ``fused_linear=True`` are the older switches
     for "nccl" / "fused".)"""
 
-    def __init__(self, model, n_slots, t_max, device, tp, graph_decode=False, decode_sum="push",
+    def __init__(self, model, n_slots, t_max, device, tp, graph_decode=False, decode_sum="arnorm",
                  peer_allreduce=None, fused_linear=None):
         if fused_linear:
             decode_sum = "fused"
         elif peer_allreduce is False:
             decode_sum = "nccl"
-        if decode_sum not in ("push", "fused", "peer", "nccl"):
+        if decode_sum not in ("arnorm", "push", "fused", "peer", "nccl"):
             raise ValueError(f"decode_sum {decode_sum!r}")
         self.decode_sum = decode_sum
-        self.peer_ar = self.peer_linear = None
+        self.peer_ar = self.peer_linear = self.peer_norm = None
         if tp > 1:
             hidden = model.config.text_config.hidden_size
             if decode_sum != "nccl":
                 self.peer_ar = enable_peer_allreduce(n_slots * hidden, device)
+            if decode_sum == "arnorm":
+                self.peer_norm = PeerAllReduceAddNorm(n_slots, hidden, device)
             if decode_sum in ("push", "fused"):
                 self.peer_linear = enable_peer_linear(n_slots, hidden, device)
                 # outside the decode step's projection + norm pairs, AllReduceLinear runs the fused
@@ -469,7 +512,8 @@ class TPEngine(CBEngine):
         """Raise if a kernel of the engine reported an error or a peer exchange timed out (a rank
         did not arrive)."""
         super().check_errors()
-        for what, inst in (("peer all-reduce", self.peer_ar), ("fused projection + all-reduce", self.peer_linear)):
+        for what, inst in (("peer all-reduce", self.peer_ar), ("fused projection + all-reduce", self.peer_linear),
+                           ("all-reduce + add + RMSNorm", self.peer_norm)):
             if inst is not None and int(inst.err.item()) != 0:
                 raise RuntimeError(f"{what} error {int(inst.err.item())} (a rank did not arrive)")
 
@@ -477,6 +521,9 @@ class TPEngine(CBEngine):
         """Collective: release the decode graphs and the peer buffers."""
         self._graphs.clear()
         self._graph_out.clear()
+        if self.peer_norm is not None:
+            self.peer_norm.close()
+            self.peer_norm = None
         if self.peer_linear is not None:
             torch.cuda.synchronize()
             if _PEER_LINEAR is self.peer_linear:

@@ -95,11 +95,12 @@ def parse():
                     help="after the model leg, profile graph-replayed decode steps (torch.profiler, device time "
                          "per kernel) and report a per-category breakdown")
     ap.add_argument("--model-gen", type=int, default=512, help="greedy tokens per turn of the model leg")
-    ap.add_argument("--model-allreduce", choices=["push", "fused", "peer", "nccl"], default="push",
-                    help="TP decode sums (TPEngine decode_sum): cuBLAS + push of the partial + residual add / RMSNorm "
-                         "summing the ranks (gdn_push_partial + gdn_pull_add_rmsnorm); the same with the tcgen05 "
-                         "projection pushing its tiles (gdn_linear_push); cuBLAS + peer-memory all-reduce; or "
-                         "cuBLAS + NCCL")
+    ap.add_argument("--model-allreduce", choices=["arnorm", "push", "fused", "peer", "nccl"], default="arnorm",
+                    help="TP decode sums (TPEngine decode_sum): cuBLAS + one kernel summing the ranks inside the "
+                         "residual add / RMSNorm (gdn_allreduce_add_rmsnorm); cuBLAS + push of the partial + "
+                         "add / RMSNorm summing the ranks (gdn_push_partial + gdn_pull_add_rmsnorm); the same with "
+                         "the tcgen05 projection pushing its tiles (gdn_linear_push); cuBLAS + peer-memory "
+                         "all-reduce; or cuBLAS + NCCL")
     return ap.parse_args()
 
 
@@ -554,6 +555,7 @@ def run_f1(world, rank, iters=64):
     import torch.distributed as dist
     fl = tp_mod.PeerLinearAllReduce(n, H, dev)
     ar = tp_mod.PeerAllReduce(n * H, dev)
+    arn = tp_mod.PeerAllReduceAddNorm(n, H, dev)
     nw = torch.ones(H, device=dev, dtype=torch.bfloat16)
     try:
         for name, k in (("o_proj / out_proj", 6144 // world), ("down_proj", 17408 // world)):
@@ -572,6 +574,10 @@ def run_f1(world, rank, iters=64):
                 fl.push(x, nxt())
                 fl.pull_add_rmsnorm(res, nw, 1e-6, out=nrm)
 
+            def cub_arnorm():
+                torch.matmul(x, nxt().t(), out=y)
+                arn(res, y, nw, 1e-6, out=nrm)
+
             def cub_push_pull():
                 torch.matmul(x, nxt().t(), out=y)
                 fl.push_partial(y)
@@ -583,7 +589,8 @@ def run_f1(world, rank, iters=64):
                  "fused_gdn_linear_allreduce": gtime(lambda: fl(x, nxt())),
                  "cublas_peer_allreduce_add_rmsnorm": gtime(cub_ar_norm),
                  "push_pull_add_rmsnorm": gtime(push_pull),
-                 "cublas_push_pull_add_rmsnorm": gtime(cub_push_pull)}
+                 "cublas_push_pull_add_rmsnorm": gtime(cub_push_pull),
+                 "cublas_allreduce_add_rmsnorm": gtime(cub_arnorm)}
             wb = H * k * 2
             link = (world - 1) * n * H * 2
             target = max(wb / (hbm * 1e9), link / 770e9) * 1e6
@@ -596,6 +603,7 @@ def run_f1(world, rank, iters=64):
     finally:
         fl.close()
         ar.close()
+        arn.close()
     return out
 
 
@@ -893,6 +901,7 @@ def run_model(args, world, rank, local):
            "timing": "wall clock per engine call (each ends with its host read of the tokens), max over ranks",
            "graph": True, "weights": "random-init bf16",
            "allreduce": ("none" if world <= 1 else {
+               "arnorm": "cuBLAS + gdn_allreduce_add_rmsnorm (peer memory) for decode, NCCL for prefill",
                "push": "cuBLAS + gdn_push_partial + gdn_pull_add_rmsnorm (peer memory) for decode, NCCL for prefill",
                "fused": "gdn_linear_push + gdn_pull_add_rmsnorm (peer memory) for decode, NCCL for prefill",
                "peer": "cuBLAS + gdn_allreduce (peer memory) for decode, NCCL for prefill",

@@ -392,6 +392,25 @@ GDN_API int gdn_linear_allreduce(const void* x, int64_t x_rs, const void* w, int
 GDN_API int gdn_linear_push(const void* x, int64_t x_rs, const void* w, int64_t w_rs, int n, int n_out, int k,
                             int splits, int rank, int world, void* const* bufs, int max_rows, int max_out,
                             int32_t* err_flag, int dtype, void* stream);
+/* gdn_allreduce_add_rmsnorm: the all-reduce of a row-parallel projection
+ * fused into its consumer, the residual add and the next RMSNorm (the
+ * dist.all_reduce of AllReduceLinear.forward, src/cb_tp.py:25-35, then x + h
+ * and Qwen3_5RMSNorm, src/cb_engine.py:295-355), one CTA per token row: this
+ * rank's partial row h[j] goes to every rank with plain stores and one flag,
+ * the other ranks' flags of the row are awaited (bounded), then x[j] =
+ * bf16(x[j] + bf16(sum of the partials in rank order)) in place and out[j] =
+ * RMSNorm(x[j]) -- bit for bit gdn_allreduce -> add -> gdn_rmsnorm.  Buffers:
+ * gdn_ar_norm_buffer_bytes(world, max_rows, dim) per rank from gdn_ar_alloc,
+ * shared by IPC like gdn_allreduce's; every call passes the same dim and
+ * max_rows >= rows.  A rank that does not arrive makes the others set
+ * *err_flag = 3 and leave x and out alone.  bf16; world >= 2.
+ */
+GDN_API size_t gdn_ar_norm_buffer_bytes(int world, int max_rows, int dim, int dtype);
+GDN_API int gdn_allreduce_add_rmsnorm(void* x, int64_t x_rs, const void* h, int64_t h_rs, const void* weight,
+                                      void* out, int64_t out_rs, int64_t rows, int dim, float eps, int rank, int world,
+                                      void* const* bufs, int max_rows, uint32_t spin_limit, int32_t* err_flag,
+                                      int dtype, void* stream);
+
 /* gdn_push_partial: the push of gdn_linear_push for a product y [n, n_out]
  * computed elsewhere (e.g. a library GEMM), same buffers, epochs and flags. */
 GDN_API int gdn_push_partial(const void* y, int64_t y_rs, int n, int n_out, int rank, int world, void* const* bufs,

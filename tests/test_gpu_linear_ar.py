@@ -11,7 +11,9 @@ narrower than the buffers; 1-128 tokens), the calls are also captured in a CUDA 
 with fresh inputs, and the result is compared with F.linear + NCCL all-reduce within bf16
 tolerance.  The push / pull split (gdn_linear_push, or a cuBLAS product pushed by gdn_push_partial,
 then gdn_pull_add_rmsnorm summing the ranks, adding the residual and normalizing) must equal the all-reduce output added to the residual in bf16
-and ops.rmsnorm BIT FOR BIT, eagerly, mixed with full fused calls, and captured in a graph.  A second
+and ops.rmsnorm BIT FOR BIT, eagerly, mixed with full fused calls, and captured in a graph; so must
+the all-reduce fused into the residual add + RMSNorm (gdn_allreduce_add_rmsnorm) against
+PeerAllReduce, the add and ops.rmsnorm, for 1-128 rows, eagerly and in a graph.  A second
 instance with a short spin limit checks the failure path: only rank 0 calls, its waits run out (in
 the fused call, and in the pull after a push), it reports error 3 and leaves y / x / out unwritten,
 while the other ranks wait in a host barrier (buffers mapped, no kernel in flight).  Skipped when fewer than two GPUs are visible.
@@ -170,12 +172,55 @@ def _rank(rank, world, port, q):
             ok &= torch.equal(pres, x2) and torch.equal(pout2, o2) and torch.equal(pout1, ops.rmsnorm(x1, nw, 1e-6))
         out["push_pull_graph"] = bool(ok)
         del graph
+        # the all-reduce fused into the residual add + RMSNorm (gdn_allreduce_add_rmsnorm): bit for
+        # bit PeerAllReduce -> x + h -> ops.rmsnorm, eagerly and in a graph, rows changing per call
+        arn = tp.PeerAllReduceAddNorm(MAX_ROWS, HIDDEN, dev)
+        par = tp.PeerAllReduce(MAX_ROWS * HIDDEN, dev)
+        ok = True
+        for case, rows in enumerate([32, 1, 128, 17, 32]):
+            g0 = torch.Generator().manual_seed(40 + case)
+            h = (torch.randn(world, rows, HIDDEN, generator=g0) * 3).to(torch.bfloat16)[rank].to(dev)
+            res0 = (torch.randn(rows, HIDDEN, generator=g0) * 2).to(torch.bfloat16).to(dev)
+            hs = h.clone()
+            par(hs)
+            ref_x = res0 + hs
+            res = res0.clone()
+            got = arn(res, h, nw, 1e-6)
+            ok &= torch.equal(res, ref_x) and torch.equal(got, ops.rmsnorm(ref_x, nw, 1e-6))
+        hb = torch.zeros(32, HIDDEN, dtype=torch.bfloat16, device=dev)
+        rb = torch.zeros(32, HIDDEN, dtype=torch.bfloat16, device=dev)
+        s.wait_stream(torch.cuda.current_stream())
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(graph, stream=s):
+                go1 = arn(rb, hb, nw, 1e-6)
+                go2 = arn(rb, hb, nw, 1e-6)
+        torch.cuda.current_stream().wait_stream(s)
+        for rep in range(3):
+            g0 = torch.Generator().manual_seed(60 + rep)
+            h = (torch.randn(world, 32, HIDDEN, generator=g0) * 3).to(torch.bfloat16)[rank].to(dev)
+            r0 = (torch.randn(32, HIDDEN, generator=g0) * 2).to(torch.bfloat16).to(dev)
+            hb.copy_(h)
+            rb.copy_(r0)
+            graph.replay()
+            torch.cuda.synchronize()
+            hs = h.clone()
+            par(hs)
+            x1 = r0 + hs
+            x2 = x1 + hs
+            ok &= torch.equal(rb, x2) and torch.equal(go1, ops.rmsnorm(x1, nw, 1e-6)) and torch.equal(
+                go2, ops.rmsnorm(x2, nw, 1e-6))
+        out["arnorm"] = bool(ok)
+        del graph
+        arn.close()
+        par.close()
         out["err"] = int(fl.err.item())
         out["applies_big"] = fl.applies(torch.zeros(MAX_ROWS + 1, 64, dtype=torch.bfloat16, device=dev),
                                         torch.zeros(64, 64, dtype=torch.bfloat16, device=dev))
         fl.close()
         # failure path: rank 0 alone calls; its bounded waits run out
         fl2 = tp.PeerLinearAllReduce(16, 1024, dev, spin_limit=20000)
+        arn2 = tp.PeerAllReduceAddNorm(16, 1024, dev, spin_limit=20000)
         if rank == 0:
             x, w = (t.to(dev) for t in inp(0, 7, 16, 1024, 512))
             y = fl2(x, w)
@@ -187,8 +232,13 @@ def _rank(rank, world, port, q):
             o = fl2.pull_add_rmsnorm(res, torch.ones(1024, dtype=torch.bfloat16, device=dev), 1e-6)
             torch.cuda.synchronize()
             out["pull_timeout"] = int(fl2.err.item()) == 3 and bool((res == 1).all())
+            o = arn2(res, torch.ones(16, 1024, dtype=torch.bfloat16, device=dev),
+                     torch.ones(1024, dtype=torch.bfloat16, device=dev), 1e-6)
+            torch.cuda.synchronize()
+            out["arnorm_timeout"] = int(arn2.err.item()) == 3 and bool((res == 1).all())
         dist.barrier()                       # the other ranks wait here while rank 0's kernel runs
         fl2.close()
+        arn2.close()
         q.put((rank, out))
     finally:
         dist.destroy_process_group()
@@ -220,6 +270,6 @@ def test_fused_linear_allreduce_multi_gpu():
     res = dict(q.get(timeout=5) for _ in range(world))
     for r in range(world):
         assert res[r]["eager"] and res[r]["same"] and res[r]["graph"] and res[r]["nccl_close"], res[r]
-        assert res[r]["push_pull"] and res[r]["push_pull_graph"], res[r]
+        assert res[r]["push_pull"] and res[r]["push_pull_graph"] and res[r]["arnorm"], res[r]
         assert res[r]["err"] == 0 and not res[r]["applies_big"], res[r]
-    assert res[0]["timeout_err"] == 3 and res[0]["pull_timeout"], res[0]
+    assert res[0]["timeout_err"] == 3 and res[0]["pull_timeout"] and res[0]["arnorm_timeout"], res[0]

@@ -5,8 +5,9 @@ over 1 KV head, so TP 2 also exercises the KV-head replication) with tp.shard_mo
 TPEngine over two prompts and four teacher-forced decode steps, eagerly (rank 0 writes the logits
 of every step) and with CUDA-graph decode (the NCCL all-reduces captured in the graphs; its tokens
 must equal the eager argmax bit for bit), for each way of summing the row-parallel projections:
-cuBLAS + push + pull/add/norm (default), cuBLAS + peer all-reduce + add/norm (bit-identical logits),
-and the tcgen05 projection pushing its tiles (gdn_linear_push).  The parent runs CBEngine on one GPU with the same model
+cuBLAS + all-reduce fused into the add/norm (default), cuBLAS + peer all-reduce + add/norm and cuBLAS
++ push + pull/add/norm (both bit-identical logits), and the tcgen05 projection pushing its tiles
+(gdn_linear_push).  The parent runs CBEngine on one GPU with the same model
 and feed and compares the logits: the all-reduce changes the summation order, so the check is
 bf16 tolerance (2e-2 relative to the logit scale), not bits.
 Skipped when fewer than two GPUs are visible.
@@ -95,15 +96,17 @@ def _rank(rank, world, port, out_path):
         # the other decode sums: cuBLAS + peer all-reduce + add/norm, and the tcgen05 projection pushing
         # its tiles (gdn_linear_push) before the pull + add + norm
         other = {}
-        for mode in ("peer", "fused"):
+        for mode in ("peer", "push", "fused"):
             lg = run(tp.TPEngine, model, dev, False, tp=world, decode_sum=mode)
             gt = run(tp.TPEngine, model, dev, True, tp=world, decode_sum=mode)
             assert gt == [x.argmax(-1).tolist() for x in lg[1:]], mode
             other[mode] = lg
         flogits = other["fused"]
-        # push (default) and peer sum the same cuBLAS partials in the same rank order: same logits
-        for a, b in zip(logits, other["peer"]):
-            assert np.array_equal(a, b)
+        # arnorm (default), push and peer sum the same cuBLAS partials in the same rank order: the same
+        # logits bit for bit
+        for mode in ("peer", "push"):
+            for a, b in zip(logits, other[mode]):
+                assert np.array_equal(a, b), mode
         # the LM head split by vocabulary (cross-rank packed argmax, captured in the graphs): the same
         # tokens wherever the eager logits' top two are not a near-tie
         vmodel = build_model(dev)
