@@ -978,17 +978,20 @@ __global__ void __launch_bounds__(128) ar_add_rmsnorm_kernel(const AddNormParams
   }
   __syncthreads();  // every thread's stores before the flag threads' system-scope release
   if (tid < p.world && tid != p.rank) st_release_sys(arflag_at(p.bufs[tid], par, p.rank, j), e);
-  const volatile int32_t* verr = p.err;
-  for (uint32_t it = 0;; ++it) {
-    const int mine = tid >= p.world || tid == p.rank || ld_relaxed_sys(arflag_at(own, par, tid, j)) == e;
-    if (__syncthreads_and(mine)) break;
-    if (__syncthreads_or(it > p.spin_limit || (verr && *verr != 0))) {
-      if (tid == 0) s_ok = 0;
-      break;
+  // only the world - 1 polling threads wait, each with acquire loads on its source's flag; the CTA
+  // barrier after them orders every thread's reads (no fence in the other threads)
+  if (tid < p.world && tid != p.rank) {
+    const uint32_t* f = arflag_at(own, par, tid, j);
+    const volatile int32_t* verr = p.err;
+    uint32_t it = 0;
+    while (ld_acquire_sys(f) != e) {
+      if (++it > p.spin_limit || (verr && *verr != 0)) {
+        s_ok = 0;
+        break;
+      }
+      __nanosleep(32);
     }
-    __nanosleep(32);
   }
-  fence_acq_rel_sys();
   __syncthreads();
   if (!s_ok) {  // a rank did not arrive: report it and leave x and out alone
     if (tid == 0 && p.err) atomicExch(p.err, 3);
