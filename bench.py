@@ -667,6 +667,11 @@ def tp_parity(world, rank, local):
     (1) The peer-memory all-reduce on the decode size [slots, hidden] bf16: bit-identical to the fp32
         sum of all ranks' inputs in rank order rounded once to bf16, and within one bf16 rounding of
         NCCL's all-reduce.
+    (3) f1, the o_proj-shaped projection fused with its sum (gdn_linear_allreduce): bit-identical to
+        the rank-order sum of each rank's gdn_linear partial with the same split count, and within
+        bf16 tolerance of the rank-order sum of cuBLAS partials; (4) the sum fused into the residual
+        add + RMSNorm (gdn_allreduce_add_rmsnorm): bit-identical to the peer all-reduce, the add and
+        gdn_rmsnorm.
     (2) A 4-layer model with the config-3 shapes (3 GDN : 1 attention, 24 q / 4 KV heads, so TP 8
         replicates KV heads; the LM head split by vocabulary): the TP engine over all ranks against
         the single-GPU engine on rank 0 with the same weights and feed (three prompts, then two
@@ -699,6 +704,57 @@ def tp_parity(world, rank, local):
     ulps = (z.float() - ref.float()).abs() / torch.clamp(ref.float().abs(), min=1e-3) * 128
     res["allreduce"] = {"shape": [slots, H], "bitexact_vs_fp32_rank_order": bit, "err_flag": ar_err,
                         "max_vs_nccl_bf16_ulps": float(ulps.max().item())}
+    # ---- (3) f1: the row-parallel projection fused with the sum (o_proj shape) and (4) the sum fused
+    # into the residual add + RMSNorm
+    ops = importlib.import_module(f"{PKG}.ops")
+    k = 6144 // world
+    gx = torch.Generator().manual_seed(950 + rank)
+    xf = torch.randn(slots, k, generator=gx).to(torch.bfloat16).to(dev)
+    wf = (torch.randn(H, k, generator=gx) / k ** 0.5).to(torch.bfloat16).to(dev)
+    fl = tp_mod.PeerLinearAllReduce(slots, H, dev)
+    yf = fl(xf, wf)
+    S = ops.linear_plan(slots, H, k, world=world)["splits"]
+
+    def rank_sum(part):
+        parts = [torch.empty_like(part) for _ in range(world)]
+        dist.all_gather(parts, part)
+        acc = torch.zeros(part.shape, dtype=torch.float32, device=dev)
+        for p_ in parts:
+            acc += p_.float()
+        return acc.to(torch.bfloat16)
+
+    exp_f = rank_sum(ops.linear(xf, wf, splits=S))
+    cub = rank_sum(torch.nn.functional.linear(xf, wf))
+    mag = rank_sum((xf.float().abs() @ wf.float().abs().t()).to(torch.bfloat16)).float()
+    torch.cuda.synchronize()
+    f_err = int(fl.err.item())
+    fl.close()
+    f_bit = bool(torch.equal(yf, exp_f)) and f_err == 0
+    f_close = bool(((yf.float() - cub.float()).abs() <= 2 ** -6 * mag + 1e-2).all())
+    res["fused_linear_allreduce"] = {"shape": [slots, H, k], "splits": S, "err_flag": f_err,
+                                     "bitexact_vs_rank_sum_of_gdn_linear": f_bit,
+                                     "within_bf16_of_cublas_rank_sum": f_close}
+    arn = tp_mod.PeerAllReduceAddNorm(slots, H, dev)
+    par = tp_mod.PeerAllReduce(slots * H, dev)
+    gh = torch.Generator().manual_seed(960)
+    hs_all = (torch.randn(world, slots, H, generator=gh) * 3).to(torch.bfloat16)
+    res0 = (torch.randn(slots, H, generator=gh) * 2).to(torch.bfloat16).to(dev)
+    nw = (torch.randn(H, generator=gh) * 0.1).to(torch.bfloat16).to(dev)
+    h = hs_all[rank].to(dev)
+    hsum = h.clone()
+    par(hsum)
+    ref_x = res0 + hsum
+    ref_o = ops.rmsnorm(ref_x, nw, 1e-6)
+    xres = res0.clone()
+    out_o = arn(xres, h, nw, 1e-6)
+    torch.cuda.synchronize()
+    a_err = int(arn.err.item())
+    arn.close()
+    par.close()
+    a_bit = bool(torch.equal(xres, ref_x)) and bool(torch.equal(out_o, ref_o)) and a_err == 0
+    res["allreduce_add_rmsnorm"] = {"shape": [slots, H], "err_flag": a_err,
+                                    "bitexact_vs_allreduce_add_rmsnorm": a_bit}
+    bit = bit and f_bit and f_close and a_bit
     # ---- (2) 4-layer model
     cfg = dict(MODEL_TEXT_CONFIG, num_hidden_layers=4,
                layer_types=["linear_attention", "linear_attention", "linear_attention", "full_attention"])
