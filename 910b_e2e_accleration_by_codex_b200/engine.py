@@ -122,9 +122,15 @@ class CBEngine:
         self._pos = torch.zeros(n_slots, dtype=torch.long, device=self.dev)
         self._slot = torch.arange(n_slots, dtype=torch.int32, device=self.dev)
         # Device error flag shared by every kernel call of the engine (0 = fine, 1 = a slot index
-        # outside the pools, 2 = a bounded wait inside a kernel ran out).  It is read back with the
+        # outside the pools, 2 = a bounded wait inside a kernel ran out, 3 = a peer exchange timed out).  It is read back with the
         # tokens each step already copies to the host, so checking it costs no extra sync.
         self._err = torch.zeros(1, dtype=torch.int32, device=self.dev)
+        # a tensor-parallel engine's peer exchanges report into the same flag (3 = a rank did not
+        # arrive in time), bound before any graph captures their calls
+        for inst in (getattr(self, "peer_ar", None), getattr(self, "peer_linear", None),
+                     getattr(self, "peer_norm", None)):
+            if inst is not None:
+                inst.err = self._err
         self.graph_decode = graph_decode
         if not hasattr(self, "peer_linear"):
             self.peer_linear = None       # TPEngine sets its tensor-parallel exchanges before this runs
@@ -276,7 +282,8 @@ class CBEngine:
         pick = getattr(head, "greedy", None)
         return pick(h) if pick is not None else head(h).argmax(-1)
 
-    _ERRORS = {1: "a slot index outside the state pools", 2: "a bounded wait inside a kernel ran out"}
+    _ERRORS = {1: "a slot index outside the state pools", 2: "a bounded wait inside a kernel ran out",
+               3: "a peer rank did not arrive in time (tensor-parallel exchange)"}
 
     def _raise_on(self, code, what):
         if code:

@@ -91,9 +91,11 @@ def parse():
     ap.add_argument("--requests", type=int, default=0,
                     help="requests of the model leg (0: one per slot; configs 3/4 name 128 / 512)")
     ap.add_argument("--model-turns", type=int, default=6, help="most turns per request of the model leg")
-    ap.add_argument("--model-profile", action="store_true",
+    ap.add_argument("--model-profile", action="store_true", default=True,
                     help="after the model leg, profile graph-replayed decode steps (torch.profiler, device time "
-                         "per kernel) and report a per-category breakdown")
+                         "per kernel) and report a per-category breakdown (default on)")
+    ap.add_argument("--no-model-profile", dest="model_profile", action="store_false",
+                    help="skip the decode breakdown of the model leg")
     ap.add_argument("--model-gen", type=int, default=512, help="greedy tokens per turn of the model leg")
     ap.add_argument("--model-allreduce", choices=["arnorm", "push", "fused", "peer", "nccl"], default="arnorm",
                     help="TP decode sums (TPEngine decode_sum): cuBLAS + one kernel summing the ranks inside the "
