@@ -667,8 +667,8 @@ def tp_parity(world, rank, local):
     """Correctness gate of the tensor-parallel path, run before the timed model leg on N > 1 ranks.
 
     (1) The peer-memory all-reduce on the decode size [slots, hidden] bf16: bit-identical to the fp32
-        sum of all ranks' inputs in rank order rounded once to bf16, and within one bf16 rounding of
-        NCCL's all-reduce.
+        sum of all ranks' inputs in rank order rounded once to bf16, and within NCCL's own bf16
+        roundings (world - 1 along its ring) of NCCL's all-reduce.
     (3) f1, the o_proj-shaped projection fused with its sum (gdn_linear_allreduce): bit-identical to
         the rank-order sum of each rank's gdn_linear partial with the same split count, and within
         bf16 tolerance of the rank-order sum of cuBLAS partials; (4) the sum fused into the residual
@@ -703,9 +703,15 @@ def tp_parity(world, rank, local):
     ar_err = int(ar.err.item())
     ar.close()
     bit = bool(torch.equal(y, ref)) and ar_err == 0
-    ulps = (z.float() - ref.float()).abs() / torch.clamp(ref.float().abs(), min=1e-3) * 128
+    # NCCL rounds its partial sums to bf16 along its ring (world - 1 roundings): compare within that
+    # many bf16 steps of the inputs' magnitude sum
+    mag = torch.zeros(slots, H)
+    for x in xs:
+        mag += x.float().abs()
+    dz = (z.float() - ref.float()).abs()
+    nccl_ok = bool((dz <= world * 2.0 ** -8 * mag.to(dev)).all())
     res["allreduce"] = {"shape": [slots, H], "bitexact_vs_fp32_rank_order": bit, "err_flag": ar_err,
-                        "max_vs_nccl_bf16_ulps": float(ulps.max().item())}
+                        "nccl_within_bf16_roundings": nccl_ok, "max_abs_vs_nccl": float(dz.max().item())}
     # ---- (3) f1: the row-parallel projection fused with the sum (o_proj shape) and (4) the sum fused
     # into the residual add + RMSNorm
     ops = importlib.import_module(f"{PKG}.ops")
