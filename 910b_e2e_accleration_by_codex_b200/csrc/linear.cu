@@ -514,10 +514,11 @@ static int launch(const void* x, int64_t x_rs, const void* w, int64_t w_rs, void
   if (n < 1 || n > kMaxTokens) return fail(GDN_ERR_ARG, "%s: n = %d tokens (1..%d)", what, n, kMaxTokens);
   if (n_out < 1 || n_out % 8) return fail(GDN_ERR_ARG, "%s: n_out = %d (a positive multiple of 8)", what, n_out);
   if (k < 1 || k % 8) return fail(GDN_ERR_ARG, "%s: k = %d (a positive multiple of 8)", what, k);
-  if (!x || !w || !y) return fail(GDN_ERR_ARG, "%s: null pointer", what);
-  if (!aligned(x, 16) || !aligned(w, 16) || !aligned(y, 16))
+  const bool writes_y = !prm.push_only;  // a push leaves its result in the exchange buffers only
+  if (!x || !w || (writes_y && !y)) return fail(GDN_ERR_ARG, "%s: null pointer", what);
+  if (!aligned(x, 16) || !aligned(w, 16) || (writes_y && !aligned(y, 16)))
     return fail(GDN_ERR_ARG, "%s: x, W and y must be 16-byte aligned", what);
-  if (x_rs < k || w_rs < k || y_rs < n_out || x_rs % 8 || w_rs % 8 || y_rs % 8)
+  if (x_rs < k || w_rs < k || x_rs % 8 || w_rs % 8 || (writes_y && (y_rs < n_out || y_rs % 8)))
     return fail(GDN_ERR_ARG, "%s: row strides (x %lld, W %lld, y %lld) must cover the rows and be multiples of 8",
                 what, (long long)x_rs, (long long)w_rs, (long long)y_rs);
   if (splits < 0 || splits > kMaxSplits) return fail(GDN_ERR_ARG, "%s: splits = %d (0 = auto, 1..8)", what, splits);
@@ -854,9 +855,7 @@ extern "C" int gdn_linear_push(const void* x, int64_t x_rs, const void* w, int64
     if (!bufs[r] || !aligned(bufs[r], 16)) return fail(GDN_ERR_ARG, "gdn_linear_push: buffer %d", r);
     prm.bufs[r] = static_cast<char*>(bufs[r]);
   }
-  // y is not written in push mode; x stands in as a valid, aligned pointer for the argument checks
-  return lin::launch(x, x_rs, w, w_rs, const_cast<void*>(x), n_out, n, n_out, k, splits, prm, as_stream(stream),
-                     "gdn_linear_push");
+  return lin::launch(x, x_rs, w, w_rs, nullptr, 0, n, n_out, k, splits, prm, as_stream(stream), "gdn_linear_push");
 }
 
 extern "C" int gdn_push_partial(const void* y, int64_t y_rs, int n, int n_out, int rank, int world,
