@@ -527,7 +527,7 @@ __global__ void __launch_bounds__(kNT, 1)
       if (tid == 0) {  // P1: [Q;K] [Q;K]^T
         tc_fence_after();
         const uint32_t id = make_idesc(128, 128, false, false);
-#pragma unroll
+#pragma unroll 1
         for (int kk = 0; kk < 8; ++kk)
           umma(tmem + T_UW + 128 * bf, desc_kmajor(qk_a, 128, kk), desc_kmajor(qk_a, 128, kk), id, kk > 0);
         umma_commit(bar_mi);
@@ -622,10 +622,10 @@ __global__ void __launch_bounds__(kNT, 1)
       if (tid == 0) {  // P2: U^T = V^T B_U^T;  P3: W^T = K^T B_W^T
         tc_fence_after();
         const uint32_t id = make_idesc(128, 64, true, false);
-#pragma unroll
+#pragma unroll 1
         for (int kk = 0; kk < 4; ++kk)
           umma(tmem + T_UW + 128 * bf, desc_mnmajor(sb + W_V, 64, kk), desc_kmajor(sb + W_BU, 64, kk), id, kk > 0);
-#pragma unroll
+#pragma unroll 1
         for (int kk = 0; kk < 4; ++kk)
           umma(tmem + T_UW + 128 * bf + 64, desc_mnmajor(qk_a + 8192, 128, kk), desc_kmajor(sb + W_BW, 64, kk), id,
                kk > 0);
@@ -683,7 +683,7 @@ __global__ void __launch_bounds__(kNT, 1)
         ph_init ^= 1u;
       }
       const float* st = reinterpret_cast<const float*>(sm + W_INIT);
-#pragma unroll
+#pragma unroll 1
       for (int part = 0; part < 4; ++part) {
         float v[32];
 #pragma unroll
@@ -710,7 +710,7 @@ __global__ void __launch_bounds__(kNT, 1)
       const int nt = cv.nt;
       {  // S^T -> bf16 copy in TMEM (A of P4/P5), S^T e^gl back into TMEM (P6 accumulates onto it); W^T tile
         const float Gl = cv.Gl;
-#pragma unroll
+#pragma unroll 1
         for (int part = 0; part < 4; ++part) {
           float sv[32];
           tmem_ld32(tmem + T_S + lane_off + 32 * part, sv);
@@ -722,7 +722,7 @@ __global__ void __launch_bounds__(kNT, 1)
           for (int j = 0; j < 32; ++j) sv[j] *= Gl;
           tmem_st32(tmem + T_S + lane_off + 32 * part, sv);
         }
-#pragma unroll
+#pragma unroll 1
         for (int half = 0; half < 2; ++half) {
           float w[32];
           tmem_ld32(tW + lane_off + 32 * half, w);
@@ -736,7 +736,7 @@ __global__ void __launch_bounds__(kNT, 1)
       if (rt == 0) {  // P4: vn^T = U^T - S^T W^T
         tc_fence_after();
         const uint32_t id = make_idesc(128, 64, false, true, true);
-#pragma unroll
+#pragma unroll 1
         for (int kk = 0; kk < 8; ++kk) umma_ts(tU, tmem + T_S16 + 8 * kk, desc_mnmajor(sb + W_WT, 128, kk), id, 1);
         umma_commit(bar_mr);
       }
@@ -744,7 +744,7 @@ __global__ void __launch_bounds__(kNT, 1)
       ph_mr ^= 1u;
       tc_fence_after();
       {  // vn^T as bf16 copies in TMEM: plain (A of vn^T QKm^T) and scaled by rk e^(gl-gc) (A of P6)
-#pragma unroll
+#pragma unroll 1
         for (int half = 0; half < 2; ++half) {
           float a[32], d[32];
           tmem_ld32(tU + lane_off + 32 * half, a);
@@ -771,12 +771,12 @@ __global__ void __launch_bounds__(kNT, 1)
       if (rt == 0) {  // P5: W = S^T Q^T, U = vn^T QKm^T;  P6: S^T += (vn . d)^T K  (A operands from TMEM)
         tc_fence_after();
         const uint32_t ia = make_idesc(128, 64, false, false);
-#pragma unroll
+#pragma unroll 1
         for (int kk = 0; kk < 8; ++kk) umma_ts(tW, tmem + T_S16 + 8 * kk, desc_kmajor(qk_a, 128, kk), ia, kk > 0);
-#pragma unroll
+#pragma unroll 1
         for (int kk = 0; kk < 4; ++kk) umma_ts(tU, tmem + T_VN16 + 8 * kk, desc_kmajor(sb + bqk, 64, kk), ia, kk > 0);
         const uint32_t ic = make_idesc(128, 128, false, true);
-#pragma unroll
+#pragma unroll 1
         for (int kk = 0; kk < 4; ++kk) umma_ts(tmem + T_S, tmem + T_VND + 8 * kk, desc_mnmajor(qk_a + 8192, 128, kk), ic, 1);
         umma_commit(bar_mr);
       }
@@ -794,12 +794,12 @@ __global__ void __launch_bounds__(kNT, 1)
          // this thread (v, t..t+1) pairs of 8 x 8 blocks (rows v, columns t), which stmatrix.trans writes as
          // 16-byte rows of t holding 8 consecutive v: 8 stores per thread and chunk instead of 64.
         const int qd = lane & 3, m = lane >> 3, kr = lane & 7;
-#pragma unroll
+#pragma unroll 1
         for (int half = 0; half < 2; ++half) {
           float2 os[4];
 #pragma unroll
           for (int j = 0; j < 4; ++j) os[j] = *reinterpret_cast<const float2*>(cv.osc + 32 * half + 8 * j + 2 * qd);
-#pragma unroll
+#pragma unroll 1
           for (int lg = 0; lg < 2; ++lg) {  // TMEM lanes (v) 32 wg + 16 lg .. + 15
             const uint32_t loff = uint32_t(32 * wg + 16 * lg) << 16;
             uint32_t a[16], c[16];
@@ -835,7 +835,7 @@ __global__ void __launch_bounds__(kNT, 1)
       } else {
         const uint8_t* ot = sm + W_WT;
         __nv_bfloat16* og = reinterpret_cast<__nv_bfloat16*>(p.out) + int64_t(h) * kD;
-#pragma unroll
+#pragma unroll 1
         for (int k8 = 0; k8 < 8; ++k8) {
           const int cidx = rt + 128 * k8, t = cidx >> 4, cc = cidx & 15;
           if (t < nt)
@@ -850,7 +850,7 @@ __global__ void __launch_bounds__(kNT, 1)
     // final state: thread v holds column v of S; a warp's store of row k covers 128 contiguous bytes
     if (p.final_pool) {
       float* dst = p.final_pool + (itm.fslot * p.Hv + h) * int64_t(kD * kD) + row;
-#pragma unroll
+#pragma unroll 1
       for (int part = 0; part < 4; ++part) {
         float v[32];
         tmem_ld32(tmem + T_S + lane_off + 32 * part, v);
