@@ -557,31 +557,27 @@ __global__ void __launch_bounds__(kNT, 1)
           const int half = hv;
           float a[32];
           tmem_ld32(tmem + T_UW + 128 * bf + lane_off + 64 + 32 * half, a);
-          if (row < 64) {
-            const int t = row;
-            const float gt = cv.gc[t], f = cv.rn[t] * scale;
+          // rows 0-63: QKm[t][s] = (q_t k_s) rq_t scale rk_s e^(gc_t - gc_s), s <= t; rows 64-127:
+          // X[i][s] = -(k_i k_s) rk_i beta_i rk_s e^(gc_i - gc_s), s < i.  One code path for both (the
+          // sign factor and the bound differ; every product is rounded as in the two separate forms).
+          const bool qrow = row < 64;
+          const int t = qrow ? row : row - 64;
+          const int lim = qrow ? t + 1 : t;
+          const float g0 = cv.gc[t], f = qrow ? cv.rn[t] * scale : cv.rn[64 + t] * cv.bt[t];
+          const float sg = qrow ? 1.f : -1.f;
 #pragma unroll
-            for (int j4 = 0; j4 < 8; ++j4) {  // the per-column vectors as 16-byte broadcast loads
-              const float4 gs = lds4(cv.gc + 32 * half + 4 * j4), rs = lds4(cv.rn + 64 + 32 * half + 4 * j4);
+          for (int j4 = 0; j4 < 8; ++j4) {  // the per-column vectors as 16-byte broadcast loads
+            const float4 gs = lds4(cv.gc + 32 * half + 4 * j4), rs = lds4(cv.rn + 64 + 32 * half + 4 * j4);
 #pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const int j = 4 * j4 + e, s = 32 * half + j;
-                a[j] = (s <= t) ? a[j] * f * f4get(rs, e) * ex2(gt - f4get(gs, e)) : 0.f;
-              }
+            for (int e = 0; e < 4; ++e) {
+              const int j = 4 * j4 + e, s = 32 * half + j;
+              a[j] = (s < lim) ? sg * (a[j] * f * f4get(rs, e)) * ex2(g0 - f4get(gs, e)) : 0.f;
             }
+          }
+          if (qrow) {
             store_row32(sm + bqk, 64, t, 4 * half, a);
           } else {
-            const int i = row - 64;
-            const float gi = cv.gc[i], f = cv.rn[64 + i] * cv.bt[i];
-#pragma unroll
-            for (int j4 = 0; j4 < 8; ++j4) {
-              const float4 gs = lds4(cv.gc + 32 * half + 4 * j4), rs = lds4(cv.rn + 64 + 32 * half + 4 * j4);
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const int j = 4 * j4 + e, s = 32 * half + j;
-                a[j] = (s < i) ? -(a[j] * f * f4get(rs, e)) * ex2(gi - f4get(gs, e)) : 0.f;
-              }
-            }
+            const int i = t;
             // 16-byte stores: lanes are rows LT floats apart, so scalar stores would hit 8 banks
 #pragma unroll
             for (int q4 = 0; q4 < 8; ++q4)
