@@ -19,6 +19,7 @@ the library's message.  There is no CPU path: CPU tensors raise.
 """
 from __future__ import annotations
 
+import ctypes
 import math
 
 import torch
@@ -483,7 +484,6 @@ def linear(x: torch.Tensor, weight: torch.Tensor, out: torch.Tensor | None = Non
 def linear_plan(n, n_out, k, splits=0, world=1):
     """The launch gdn_linear (world 1) / gdn_linear_allreduce (world > 1) makes for this shape:
     dict(splits, stages, smem, tiles, kblocks)."""
-    import ctypes
     out = (ctypes.c_int32 * 5)()
     _lib.check(_lib.load().gdn_linear_plan(n, n_out, k, splits, world, out), "gdn_linear_plan")
     return dict(zip(("splits", "stages", "smem", "tiles", "kblocks"), list(out)))
