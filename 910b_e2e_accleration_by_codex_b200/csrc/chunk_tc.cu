@@ -168,6 +168,7 @@ __device__ __forceinline__ void tri_inverse64(float* X, float* P, int warp, int 
     const int m = warp >> 2, c = lane & 15, lo = m * 32, hi = lo + 16;
     const int rg = m == 0 ? (warp & 3) : 3 - (warp & 3), r0 = 4 * rg + 2 * (lane >> 4);
     float a[2] = {0.f, 0.f};
+#pragma unroll 4
     for (int tq = 0; tq <= rg; ++tq) {  // B = T(hi, hi) is lower triangular: columns < 4 (rg + 1)
       float x[4];
 #pragma unroll
@@ -203,6 +204,7 @@ __device__ __forceinline__ void tri_inverse64(float* X, float* P, int warp, int 
     {  // P = T(32:64, 32:64) X(32:64, 0:32): column c = lane, rows 4g .. 4g+3, columns of B below 4 (g + 1)
       const int c = lane, r0 = 4 * g;
       float a[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
       for (int tq = 0; tq <= g; ++tq) {
         float x[4];
 #pragma unroll
@@ -222,6 +224,7 @@ __device__ __forceinline__ void tri_inverse64(float* X, float* P, int warp, int 
        // loads), the T rows are uniform across the warp (broadcast), the result leaves as one 16-byte store.
       const int r = lane, c0 = 4 * g;
       float b[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
       for (int k4 = g; k4 < 8; ++k4) {
         const float4 pv = lds4(P + r * LP + 4 * k4);
 #pragma unroll
