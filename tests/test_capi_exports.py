@@ -96,6 +96,75 @@ def test_validation_errors_without_gpu(lib):
     assert rc == 1 and b"rank" in lib.gdn_last_error()
 
 
+def test_decode_projection_and_glue_validation_without_gpu(lib):
+    """The f1 projections, the peer exchanges around them and the decode-step glue reject bad
+    arguments before any CUDA call (pointers here are never dereferenced)."""
+    L = pkg("_lib")
+    ok, odd = 4096, 4096 + 2
+    BF, F32 = L.GDN_BF16, L.GDN_F32
+    table = (ctypes.c_void_p * 2)(ok, ok)
+
+    def rejects(rc, code, text):
+        assert rc == code, (rc, lib.gdn_last_error())
+        assert text in lib.gdn_last_error(), lib.gdn_last_error()
+
+    # gdn_linear: tokens 1..256, n_out and k multiples of 8, 16-byte alignment, strides, split count
+    rejects(lib.gdn_linear(ok, 64, ok, 64, ok, 64, 0, 64, 64, 0, BF, None, None), 1, b"tokens")
+    rejects(lib.gdn_linear(ok, 64, ok, 64, ok, 64, 257, 64, 64, 0, BF, None, None), 1, b"tokens")
+    rejects(lib.gdn_linear(ok, 64, ok, 64, ok, 64, 8, 60, 64, 0, BF, None, None), 1, b"n_out")
+    rejects(lib.gdn_linear(ok, 64, ok, 64, ok, 64, 8, 64, 60, 0, BF, None, None), 1, b"k =")
+    rejects(lib.gdn_linear(odd, 64, ok, 64, ok, 64, 8, 64, 64, 0, BF, None, None), 1, b"aligned")
+    rejects(lib.gdn_linear(ok, 60, ok, 64, ok, 64, 8, 64, 56, 0, BF, None, None), 1, b"strides")
+    rejects(lib.gdn_linear(ok, 64, ok, 64, ok, 64, 8, 64, 64, 9, BF, None, None), 1, b"splits")
+    rejects(lib.gdn_linear(ok, 64, ok, 64, ok, 64, 8, 64, 64, 0, F32, None, None), 3, b"bf16")
+    plan = (ctypes.c_int32 * 5)()
+    rejects(lib.gdn_linear_plan(0, 64, 64, 0, 1, plan), 1, b"gdn_linear_plan")
+    # exchange buffers: world 1..8, rows 1..256, widths multiples of 8
+    assert lib.gdn_linear_ar_buffer_bytes(9, 16, 5120, BF) == 0
+    assert lib.gdn_linear_ar_buffer_bytes(2, 0, 5120, BF) == 0
+    assert lib.gdn_linear_ar_buffer_bytes(2, 16, 5124, BF) == 0
+    assert lib.gdn_linear_ar_buffer_bytes(2, 16, 5120, BF) > 2 * 2 * 16 * 5120 * 2
+    assert lib.gdn_ar_norm_buffer_bytes(9, 16, 5120, BF) == 0
+    assert lib.gdn_ar_norm_buffer_bytes(2, 300, 5120, BF) == 0
+    assert lib.gdn_ar_norm_buffer_bytes(2, 16, 5120, BF) > 2 * 2 * 16 * 5120 * 2
+    # fused projection + sum, and its push / pull halves
+    rejects(lib.gdn_linear_allreduce(ok, 64, ok, 64, ok, 64, 8, 64, 64, 0, 2, 2, table, 16, 64, 0, None, BF, None),
+            1, b"rank")
+    rejects(lib.gdn_linear_allreduce(ok, 64, ok, 64, ok, 64, 32, 64, 64, 0, 0, 2, table, 16, 64, 0, None, BF, None),
+            1, b"buffer rows")
+    rejects(lib.gdn_linear_allreduce(ok, 64, ok, 64, ok, 64, 8, 128, 64, 0, 0, 2, table, 16, 64, 0, None, BF, None),
+            1, b"does not fit")
+    rejects(lib.gdn_linear_allreduce(ok, 64, ok, 64, ok, 64, 8, 64, 64, 0, 0, 2, None, 16, 64, 0, None, BF, None),
+            1, b"buffer table")
+    rejects(lib.gdn_linear_push(ok, 64, ok, 64, 8, 64, 64, 0, 0, 1, table, 16, 64, None, BF, None), 1, b"world")
+    rejects(lib.gdn_push_partial(ok, 64, 8, 64, 0, 1, table, 16, 64, BF, None), 1, b"world")
+    rejects(lib.gdn_push_partial(ok, 64, 32, 64, 0, 2, table, 16, 64, BF, None), 1, b"does not fit")
+    rejects(lib.gdn_pull_add_rmsnorm(ok, 64, ok, ok, 64, 4, 7, 1e-6, 0, 2, table, 16, 64, 0, None, BF, None), 1,
+            b"dim")
+    rejects(lib.gdn_pull_add_rmsnorm(ok, 64, ok, ok, 64, 4, 64, 1e-6, 0, 1, table, 16, 64, 0, None, BF, None), 1,
+            b"world")
+    rejects(lib.gdn_allreduce_add_rmsnorm(ok, 64, ok, 64, ok, ok, 64, 4, 64, 1e-6, 0, 1, table, 16, 0, None, BF,
+                                          None), 1, b"world")
+    rejects(lib.gdn_allreduce_add_rmsnorm(ok, 64, ok, 64, ok, ok, 64, 32, 64, 1e-6, 0, 2, table, 16, 0, None, BF,
+                                          None), 1, b"rows")
+    # decode-step glue
+    rejects(lib.gdn_add_rmsnorm(ok, 64, ok, 64, ok, ok, 64, 4, 7, 1e-6, BF, None), 1, b"dim")
+    rejects(lib.gdn_add_rmsnorm(ok, 64, odd, 64, ok, ok, 64, 4, 64, 1e-6, BF, None), 1, b"h rows")
+    rejects(lib.gdn_add_rmsnorm(ok, 64, ok, 64, ok, ok, 64, 4, 64, 1e-6, F32, None), 3, b"bf16")
+    rejects(lib.gdn_silu_mul(ok, 128, 7, ok, 64, 4, BF, None), 1, b"inter")
+    rejects(lib.gdn_silu_mul(ok, 100, 64, ok, 64, 4, BF, None), 1, b"aligned")
+    rejects(lib.gdn_silu_mul(ok, 128, 64, ok, 64, 4, F32, None), 3, b"bf16")
+    assert lib.gdn_silu_mul(ok, 128, 64, ok, 64, 0, BF, None) == 0                      # no rows: no-op
+    rejects(lib.gdn_attn_decode_prep(ok, 16384, ok, ok, 1e-6, ok, ok, 64, 64, ok, ok, ok, ok, 4, 24, 4, 300, BF,
+                                     None), 1, b"hd")
+    rejects(lib.gdn_attn_decode_prep(ok, 16384, ok, ok, 1e-6, ok, ok, 64, 24, ok, ok, ok, ok, 4, 24, 4, 256, BF,
+                                     None), 1, b"rd")
+    rejects(lib.gdn_attn_decode_prep(ok, 100, ok, ok, 1e-6, ok, ok, 64, 64, ok, ok, ok, ok, 4, 24, 4, 256, BF,
+                                     None), 1, b"strides")
+    rejects(lib.gdn_attn_decode_prep(ok, 16384, ok, ok, 1e-6, ok, ok, 64, 64, ok, ok, ok, ok, 4, 24, 4, 256, F32,
+                                     None), 3, b"bf16")
+
+
 def test_ops_refuse_cpu_tensors():
     import torch
     ops = pkg("ops")
