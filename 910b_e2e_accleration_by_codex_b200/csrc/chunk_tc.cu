@@ -123,8 +123,9 @@ __device__ __forceinline__ void group_sync(int id) {
 // operand a uniform-address float4; in the last product P A a lane owns one output row (P rows are
 // LP floats apart, so their 16-byte loads do not conflict) and the A rows are uniform-address.
 __device__ __forceinline__ void tri_inverse64(float* X, float* P, int warp, int lane) {
-  if (warp < 4) {  // diagonal block `warp`; lane j < 16 owns column j
-    const int b0 = 16 * warp, j = lane & 15;
+  if (warp < 2) {  // diagonal block 2 warp + lane / 16; lane j = lane % 16 owns column j (the two half-warps'
+                   // blocks are 16 banks apart, so their accesses do not conflict)
+    const int b0 = 16 * (2 * warp + (lane >> 4)), j = lane & 15;
     float acc[16], r[16];
 #pragma unroll
     for (int i = 0; i < 16; ++i) acc[i] = lds1(X + (b0 + i) * LT + b0 + j);
@@ -152,10 +153,8 @@ __device__ __forceinline__ void tri_inverse64(float* X, float* P, int warp, int 
       }
     }
     __syncwarp();
-    if (lane < 16) {
 #pragma unroll
-      for (int i = 0; i < 16; ++i) X[(b0 + i) * LT + b0 + j] = i == j ? 1.f : (i > j ? r[i] : 0.f);
-    }
+    for (int i = 0; i < 16; ++i) X[(b0 + i) * LT + b0 + j] = i == j ? 1.f : (i > j ? r[i] : 0.f);
   }
   group_sync(1);
   // In both merge levels the first product B X21 has a lower-triangular left factor B, so the rows of
@@ -541,9 +540,14 @@ __global__ void __launch_bounds__(kNT, 1)
       if (hv == 0) {  // l2-norm factors from the diagonal (bf16 arithmetic as the reference's l2norm)
         float dg[32];
         tmem_ld32(tmem + T_UW + 128 * bf + lane_off + 32 * wg, dg);
-        float ss = dg[0];
+        // dg[lane] by a select tree over the lane's bits (31 selects)
 #pragma unroll
-        for (int j = 1; j < 32; ++j) ss = j == lane ? dg[j] : ss;
+        for (int w = 16; w >= 1; w >>= 1) {
+          const bool hi = (lane & w) != 0;
+#pragma unroll
+          for (int j = 0; j < w; ++j) dg[j] = hi ? dg[j + w] : dg[j];
+        }
+        const float ss = dg[0];
         float inv = 1.f;
         if (p.l2norm) inv = bf16r(1.0f / sqrtf(bf16r(bf16r(ss) + 1e-6f)));
         cv.rn[row] = (row & 63) < nt ? inv : 0.f;
