@@ -553,12 +553,6 @@ __global__ void __launch_bounds__(kNT, 1)
         cv.rn[row] = (row & 63) < nt ? inv : 0.f;
       }
       group_sync(1);
-      if (tid < 64) {
-        const float rk = cv.rn[64 + tid];
-        cv.dkd[tid] = rk * ex2(cv.gl - cv.gc[tid]);
-        cv.bwc[tid] = cv.bt[tid] * cv.egc[tid] * rk;
-        cv.osc[tid] = cv.rn[tid] * scale * cv.egc[tid];
-      }
       {  // P1 epilogue: QKm tile (rows 0-63) and X (rows 64-127), from the K columns 64-127
         {
           const int half = hv;
@@ -570,15 +564,15 @@ __global__ void __launch_bounds__(kNT, 1)
           const bool qrow = row < 64;
           const int t = qrow ? row : row - 64;
           const int lim = qrow ? t + 1 : t;
-          const float g0 = cv.gc[t], f = qrow ? cv.rn[t] * scale : cv.rn[64 + t] * cv.bt[t];
-          const float sg = qrow ? 1.f : -1.f;
+          // the X rows' minus sign rides on f (negation is exact: same values as negating each product)
+          const float g0 = cv.gc[t], f = qrow ? cv.rn[t] * scale : -(cv.rn[64 + t] * cv.bt[t]);
 #pragma unroll
           for (int j4 = 0; j4 < 8; ++j4) {  // the per-column vectors as 16-byte broadcast loads
             const float4 gs = lds4(cv.gc + 32 * half + 4 * j4), rs = lds4(cv.rn + 64 + 32 * half + 4 * j4);
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
               const int j = 4 * j4 + e, s = 32 * half + j;
-              a[j] = (s < lim) ? sg * (a[j] * f * f4get(rs, e)) * ex2(g0 - f4get(gs, e)) : 0.f;
+              a[j] = (s < lim) ? (a[j] * f * f4get(rs, e)) * ex2(g0 - f4get(gs, e)) : 0.f;
             }
           }
           if (qrow) {
@@ -594,6 +588,14 @@ __global__ void __launch_bounds__(kNT, 1)
         }
       }
       group_sync(1);
+      if (warp == 2 || warp == 3) {  // per-chunk vectors of the later phases, beside the inverse's diagonal
+                                     // blocks (warps 0-1); first read after the inverse
+        const int i = tid - 64;
+        const float rk = cv.rn[64 + i];
+        cv.dkd[i] = rk * ex2(cv.gl - cv.gc[i]);
+        cv.bwc[i] = cv.bt[i] * cv.egc[i] * rk;
+        cv.osc[i] = cv.rn[i] * scale * cv.egc[i];
+      }
       tri_inverse64(Xs, Ps, warp, lane);
       {  // B_U = T diag(beta), B_W = T diag(beta e^gc rk): thread -> row t, 16 columns
         const int t = tid >> 2, cb = (tid & 3) * 16;
