@@ -557,22 +557,27 @@ __global__ void __launch_bounds__(kNT, 1)
         {
           const int half = hv;
           float a[32];
-          tmem_ld32(tmem + T_UW + 128 * bf + lane_off + 64 + 32 * half, a);
           // rows 0-63: QKm[t][s] = (q_t k_s) rq_t scale rk_s e^(gc_t - gc_s), s <= t; rows 64-127:
           // X[i][s] = -(k_i k_s) rk_i beta_i rk_s e^(gc_i - gc_s), s < i.  One code path for both (the
           // sign factor and the bound differ; every product is rounded as in the two separate forms).
           const bool qrow = row < 64;
           const int t = qrow ? row : row - 64;
           const int lim = qrow ? t + 1 : t;
-          // the X rows' minus sign rides on f (negation is exact: same values as negating each product)
-          const float g0 = cv.gc[t], f = qrow ? cv.rn[t] * scale : -(cv.rn[64 + t] * cv.bt[t]);
+          if (half == 1 && (wg & 1) == 0) {  // rows t < 32, columns s >= 32: all above the diagonal
 #pragma unroll
-          for (int j4 = 0; j4 < 8; ++j4) {  // the per-column vectors as 16-byte broadcast loads
-            const float4 gs = lds4(cv.gc + 32 * half + 4 * j4), rs = lds4(cv.rn + 64 + 32 * half + 4 * j4);
+            for (int j = 0; j < 32; ++j) a[j] = 0.f;
+          } else {
+            tmem_ld32(tmem + T_UW + 128 * bf + lane_off + 64 + 32 * half, a);
+            // the X rows' minus sign rides on f (negation is exact: same values as negating each product)
+            const float g0 = cv.gc[t], f = qrow ? cv.rn[t] * scale : -(cv.rn[64 + t] * cv.bt[t]);
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int j = 4 * j4 + e, s = 32 * half + j;
-              a[j] = (s < lim) ? (a[j] * f * f4get(rs, e)) * ex2(g0 - f4get(gs, e)) : 0.f;
+            for (int j4 = 0; j4 < 8; ++j4) {  // the per-column vectors as 16-byte broadcast loads
+              const float4 gs = lds4(cv.gc + 32 * half + 4 * j4), rs = lds4(cv.rn + 64 + 32 * half + 4 * j4);
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const int j = 4 * j4 + e, s = 32 * half + j;
+                a[j] = (s < lim) ? (a[j] * f * f4get(rs, e)) * ex2(g0 - f4get(gs, e)) : 0.f;
+              }
             }
           }
           if (qrow) {
@@ -597,18 +602,25 @@ __global__ void __launch_bounds__(kNT, 1)
         cv.osc[i] = cv.rn[i] * scale * cv.egc[i];
       }
       tri_inverse64(Xs, Ps, warp, lane);
-      {  // B_U = T diag(beta), B_W = T diag(beta e^gc rk): thread -> row t, 16 columns
-        const int t = tid >> 2, cb = (tid & 3) * 16;
+      {  // B_U = T diag(beta), B_W = T diag(beta e^gc rk): warp -> 16 columns cb, lane -> row t.  Rows 0-31
+         // of columns 32-63 lie above T's diagonal (warps 5 and 7, one per scheduler with the P1
+         // epilogue's zero warps 4 and 6): zeros without loads.
+        const int cb = 16 * (warp >> 1), t = 32 * (1 - (warp & 1)) + lane;
         float u[16], w[16];
+        if (cb >= 32 && t < 32) {
 #pragma unroll
-        for (int e4 = 0; e4 < 4; ++e4) {
-          const float4 tv4 = lds4(Xs + t * LT + cb + 4 * e4);
-          const float4 bt4 = lds4(cv.bt + cb + 4 * e4), bw4 = lds4(cv.bwc + cb + 4 * e4);
+          for (int e = 0; e < 16; ++e) u[e] = w[e] = 0.f;
+        } else {
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float tv = f4get(tv4, e);
-            u[4 * e4 + e] = tv * f4get(bt4, e);
-            w[4 * e4 + e] = tv * f4get(bw4, e);
+          for (int e4 = 0; e4 < 4; ++e4) {
+            const float4 tv4 = lds4(Xs + t * LT + cb + 4 * e4);
+            const float4 bt4 = lds4(cv.bt + cb + 4 * e4), bw4 = lds4(cv.bwc + cb + 4 * e4);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float tv = f4get(tv4, e);
+              u[4 * e4 + e] = tv * f4get(bt4, e);
+              w[4 * e4 + e] = tv * f4get(bw4, e);
+            }
           }
         }
         store_row16(sm + W_BU, 64, t, cb >> 3, u);
