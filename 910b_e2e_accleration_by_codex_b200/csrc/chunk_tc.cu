@@ -102,6 +102,11 @@ __device__ __forceinline__ float4 lds4(const float* p) {
                : "r"(smem_u32(p)));
   return v;
 }
+__device__ __forceinline__ float2 lds2(const float* p) {
+  float2 v;
+  asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(smem_u32(p)));
+  return v;
+}
 __device__ __forceinline__ float lds1(const float* p) {
   float v;
   asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(smem_u32(p)));
@@ -181,21 +186,24 @@ __device__ __forceinline__ void tri_inverse64(float* X, float* P, int warp, int 
 #pragma unroll
     for (int rr = 0; rr < 2; ++rr) P[m * 16 * LP + (r0 + rr) * LP + c] = a[rr];
     group_sync(1);
-    a[0] = 0.f;
-    a[1] = 0.f;
+    // second product T21 = P A of both merges: lane -> row (lanes 0-15 merge 0, 16-31 merge 1; P rows are
+    // LP floats apart, conflict-free 16-byte loads), warp -> columns 2 g2, 2 g2 + 1 with g2 = warp or
+    // 11 - warp (the warps sharing a scheduler split the triangle evenly).  A = T(lo, lo) is lower
+    // triangular, so only k >= 4 (g2 / 2) contribute: the skipped terms are exact zeros after a +0 start.
+    const int g2 = warp < 4 ? warp : 11 - warp, mm = lane >> 4, rm = lane & 15, lo2 = 32 * mm, c2 = 2 * g2;
+    float b0 = 0.f, b1 = 0.f;
+#pragma unroll 4
+    for (int k4 = g2 >> 1; k4 < 4; ++k4) {
+      const float4 pv = lds4(P + lane * LP + 4 * k4);
 #pragma unroll
-    for (int tq = 0; tq < 4; ++tq) {
-      float x[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) x[u] = lds1(X + (lo + 4 * tq + u) * LT + lo + c);
-#pragma unroll
-      for (int rr = 0; rr < 2; ++rr) {
-        const float4 pv = lds4(P + m * 16 * LP + (r0 + rr) * LP + 4 * tq);
-        a[rr] = fmaf(pv.w, x[3], fmaf(pv.z, x[2], fmaf(pv.y, x[1], fmaf(pv.x, x[0], a[rr]))));
+      for (int u = 0; u < 4; ++u) {
+        const float2 av = lds2(X + (lo2 + 4 * k4 + u) * LT + lo2 + c2);
+        const float pk = f4get(pv, u);
+        b0 = fmaf(pk, av.x, b0);
+        b1 = fmaf(pk, av.y, b1);
       }
     }
-#pragma unroll
-    for (int rr = 0; rr < 2; ++rr) X[(hi + r0 + rr) * LT + lo + c] = a[rr];
+    *reinterpret_cast<float2*>(X + (lo2 + 16 + rm) * LT + lo2 + c2) = make_float2(b0, b1);
     group_sync(1);
   }
   {  // level 2: group g = warp (warps 0-3) or 11 - warp (warps 4-7)
