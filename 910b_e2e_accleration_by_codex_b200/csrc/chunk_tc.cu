@@ -122,11 +122,13 @@ __device__ __forceinline__ void group_sync(int id) {
 
 // T = (I - X)^-1 for the strictly lower 64x64 X held in fp32 shared memory (row stride LT), in
 // place, by the blocked scheme of src/gdn_chunk_fast.py:33-62: 16x16 diagonal blocks by the row
-// recurrence (evaluated column-wise), then pairwise merges T21 = (B X21) A.  Run by the 8 warps of
-// the intra group (named barrier 1); P is 32 x LP floats of scratch.  In the products B X21 a lane
-// owns one output column: the column operand is one conflict-free 32-bit load per row and the row
-// operand a uniform-address float4; in the last product P A a lane owns one output row (P rows are
-// LP floats apart, so their 16-byte loads do not conflict) and the A rows are uniform-address.
+// recurrence (evaluated column-wise, on warps 0-1, one block per half-warp), then pairwise merges
+// T21 = (B X21) A.  Run by the 8 warps of the intra group (named barrier 1); P is 32 x LP floats of
+// scratch.  In the products B X21 a lane owns one output column: the column operand is one
+// conflict-free 32-bit load per row and the row operand a uniform-address float4; in the products P A
+// a lane owns one output row (P rows are LP floats apart, so their 16-byte loads do not conflict), the
+// A rows are uniform-address, and a warp owns a few output columns, so whole warps skip the k-steps
+// where A's columns are zero.
 __device__ __forceinline__ void tri_inverse64(float* X, float* P, int warp, int lane) {
   if (warp < 2) {  // diagonal block 2 warp + lane / 16; lane j = lane % 16 owns column j (the two half-warps'
                    // blocks are 16 banks apart, so their accesses do not conflict)
