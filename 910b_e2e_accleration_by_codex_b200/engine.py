@@ -55,6 +55,14 @@ def fuse_linears(mods):
     return W, [w.shape[0] for w in ws]
 
 
+def _check_slots(what, slots):
+    """Each slot at most once per call: two prompts (or two decode entries) on one slot would write
+    its pool rows from two sequences at once.  Slot indices outside the pools are left to the
+    kernels, which flag them on the device (error 1) and touch no pool row."""
+    if len(set(int(s) for s in slots)) != len(slots):
+        raise ValueError(f"{what}: a slot appears more than once in {list(slots)}")
+
+
 class CBEngine:
     def __init__(self, model, n_slots, t_max, device, graph_decode=False, tp=1):
         from transformers.models.qwen3_5 import modeling_qwen3_5 as M
@@ -233,7 +241,7 @@ class CBEngine:
         """A layer's output projection, the residual add and the next RMSNorm of the decode step:
         x <- x + proj(a) in place; returns norm(x).  With a tensor-parallel exchange (``peer_linear``,
         set by TPEngine) the sum over ranks runs inside the add + norm kernel
-        (gdn_allreduce_add_rmsnorm), or the projection pushes this rank's partial to every rank (gdn_linear_push)
+        (gdn_allreduce_add_rmsnorm), or the projection pushes this rank's partial to every rank
         (gdn_linear_push, or a cuBLAS GEMM and gdn_push_partial) and one kernel sums the ranks'
         partials, adds and normalizes (gdn_pull_add_rmsnorm);
         otherwise the projection's own forward (cuBLAS, plus the all-reduce of AllReduceLinear under
@@ -300,6 +308,9 @@ class CBEngine:
         computed (dense, as the reference); slots not in ``slots`` write their GDN update to the
         scratch row, so their conv/recurrent state is untouched (``hold`` is accepted for
         interface parity with TPEngine.decode_step and needs no save/restore)."""
+        _check_slots("decode_step", slots)
+        if len(tokens) != len(slots):
+            raise ValueError(f"decode_step: {len(tokens)} tokens for {len(slots)} slots")
         N = self.N
         tok_full = [0] * N
         slot_map = [N] * N
@@ -379,6 +390,7 @@ class CBEngine:
         """Prefill several prompts in one packed forward (no padding).  ``starts`` (optional)
         continues sequences whose first ``starts[b]`` tokens are already in their slot (chunked
         prefill).  Returns the greedy next token per prompt."""
+        _check_slots("prefill_batch", slots)
         B = len(slots)
         starts = [0] * B if starts is None else [int(s) for s in starts]
         ids = [x.reshape(-1).to(self.dev) for x in id_list]
